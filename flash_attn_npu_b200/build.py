@@ -1,0 +1,122 @@
+"""Build the sm_100a shared library `libfa_sm100.so` in-tree with nvcc.
+
+The library is a plain C-ABI shared object (see include/fa_fwd_sm100.h); it has no PyTorch
+dependency, so it is compiled directly with nvcc rather than through torch's extension
+machinery.  The five head-dimension translation units compile in parallel.
+
+Usage:  python -m flash_attn_npu_b200.build [--force] [--verbose]
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import hashlib
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent
+REPO_DIR = PKG_DIR.parent
+CSRC = PKG_DIR / "csrc"
+INCLUDE = REPO_DIR / "include"
+BUILD_DIR = REPO_DIR / "_build" / "fa_sm100"
+LIB_NAME = "libfa_sm100.so"
+LIB_PATH = PKG_DIR / LIB_NAME
+
+SOURCES = [
+    "fa_fwd_api.cu",
+    "fa_fwd_d16.cu",
+    "fa_fwd_d32.cu",
+    "fa_fwd_d64.cu",
+    "fa_fwd_d128.cu",
+    "fa_fwd_d256.cu",
+]
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+COMMON_FLAGS = [
+    "-O3",
+    "-lineinfo",
+    "-std=c++17",
+    "-Xcompiler",
+    "-fPIC",
+    "-Xcompiler",
+    "-fvisibility=hidden",
+    "--expt-relaxed-constexpr",
+]
+
+
+def nvcc_path() -> str:
+    cand = os.environ.get("NVCC") or shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not Path(cand).exists():
+        raise RuntimeError("nvcc not found; the sm_100a library cannot be built")
+    return cand
+
+
+def _inputs_digest(extra_flags: list[str]) -> str:
+    h = hashlib.sha256()
+    for p in sorted(list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h"))
+                    + list(INCLUDE.glob("*.h"))):
+        h.update(p.name.encode())
+        h.update(p.read_bytes())
+    h.update(" ".join(ARCH_FLAGS + COMMON_FLAGS + extra_flags).encode())
+    return h.hexdigest()
+
+
+def _stamp_path() -> Path:
+    return PKG_DIR / (LIB_NAME + ".sha256")
+
+
+def is_up_to_date(extra_flags: list[str] | None = None) -> bool:
+    stamp = _stamp_path()
+    return LIB_PATH.exists() and stamp.exists() and stamp.read_text().strip() == _inputs_digest(
+        extra_flags or [])
+
+
+def _compile_one(nvcc: str, src: str, extra: list[str], verbose: bool) -> Path:
+    obj = BUILD_DIR / (Path(src).stem + ".o")
+    cmd = [nvcc, *ARCH_FLAGS, *COMMON_FLAGS, *extra, "-I", str(INCLUDE), "-c", str(CSRC / src),
+           "-o", str(obj)]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {src}:\n{res.stdout}\n{res.stderr}")
+    if verbose and (res.stdout or res.stderr):
+        print(res.stdout + res.stderr)
+    return obj
+
+
+def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None) -> Path:
+    """Compile every CUDA source for sm_100a and link `libfa_sm100.so` next to this file."""
+    extra = list(extra_flags or [])
+    if not force and is_up_to_date(extra):
+        return LIB_PATH
+    nvcc = nvcc_path()
+    BUILD_DIR.mkdir(parents=True, exist_ok=True)
+    workers = min(len(SOURCES), max(1, os.cpu_count() or 1))
+    with cf.ThreadPoolExecutor(max_workers=workers) as ex:
+        objs = list(ex.map(lambda s: _compile_one(nvcc, s, extra, verbose), SOURCES))
+    tmp = LIB_PATH.with_suffix(".so.tmp")
+    cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *[str(o) for o in objs]]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, LIB_PATH)
+    _stamp_path().write_text(_inputs_digest(extra) + "\n")
+    return LIB_PATH
+
+
+def main(argv: list[str] | None = None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--verbose", action="store_true", help="print ptxas register/spill report")
+    args = ap.parse_args(argv)
+    path = build(force=args.force, verbose=args.verbose)
+    print(path)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,285 @@
+// C-ABI front end of the sm_100a FlashAttention forward (declared in include/fa_fwd_sm100.h).
+//
+// Host-side duties, in the order the reference's launcher performs them
+// (`_launch_kernel`, flash_attention_forward.py:1130-1194):
+//   validate shapes / head_dim (reference `_validate_inputs`, :1114-1122)
+//   resolve the tile config (reference `_resolve_tiling`, :626-631)
+//   size the grid (reference `_build_grid`, :1125-1127)
+//   launch on the caller's stream (reference `_attn_fwd[grid](...)`, :1159-1193)
+// plus what TMA needs: one CUtensorMap per tensor, encoded through the driver entry point
+// obtained from the runtime (no link against libcuda).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/fa_fwd_sm100.h"
+#include "fa_launch.h"
+
+namespace {
+
+constexpr int kSmemLimit = 232448;  // 227 KiB opt-in dynamic shared memory per block (sm_100)
+constexpr int kMaxStagesAllowed = 8;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// Per-device "is this an sm_100 part" cache (16 devices is plenty for one node).
+int device_ok(int dev) {
+  static int cache[16] = {0};  // 0 unknown, 1 ok, -1 not ok
+  if (dev < 0 || dev >= 16) return 0;
+  if (cache[dev] == 0) {
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return 0;
+    }
+    cache[dev] = (major == 10 && minor == 0) ? 1 : -1;
+  }
+  return cache[dev] == 1;
+}
+
+int elt_bytes(int dtype) { return dtype == FA_DTYPE_FP32 ? 4 : 2; }
+
+bool head_dim_ok(int64_t d) { return d == 16 || d == 32 || d == 64 || d == 128 || d == 256; }
+
+fa::KernelInfo info_for(int64_t head_dim, int dtype, int block_n, int qt) {
+  switch (head_dim) {
+    case 16: return fa::info_d16(dtype, block_n, qt);
+    case 32: return fa::info_d32(dtype, block_n, qt);
+    case 64: return fa::info_d64(dtype, block_n, qt);
+    case 128: return fa::info_d128(dtype, block_n, qt);
+    case 256: return fa::info_d256(dtype, block_n, qt);
+    default: return fa::KernelInfo{false, 0, 0, 0, 0, 0, 0};
+  }
+}
+
+int max_stages_for(const fa::KernelInfo& ki) {
+  if (!ki.exists) return 0;
+  const int s = (kSmemLimit - ki.smem_fixed) / ki.kv_tile_bytes;
+  return std::min(s, kMaxStagesAllowed);
+}
+
+// Encode a 4-D tiled map over a [B, H, S, D] tensor with dims listed innermost first.
+int encode_map(CUtensorMap* map, const void* ptr, int dtype, int64_t B, int64_t H, int64_t S,
+               int64_t D, const int64_t st[3], int box_cols, int box_rows, int swz_bytes) {
+  const int eb = elt_bytes(dtype);
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return FA_ERR_MISALIGNED;
+  // element strides -> byte strides for (seq, head, batch); size-1 dims get a harmless value
+  int64_t s_seq = st[2] * eb, s_head = st[1] * eb, s_batch = st[0] * eb;
+  if (S == 1) s_seq = ((D * eb + 15) / 16) * 16;
+  if (H == 1) s_head = s_seq * S;
+  if (B == 1) s_batch = s_head * H;
+  for (int64_t s : {s_seq, s_head, s_batch})
+    if (s <= 0 || s % 16 != 0 || s >= (int64_t{1} << 40)) return FA_ERR_MISALIGNED;
+  auto enc = encode_fn();
+  if (!enc) return FA_ERR_TENSOR_MAP;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S),
+                              static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_seq), static_cast<cuuint64_t>(s_head),
+                                 static_cast<cuuint64_t>(s_batch)};
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows),
+                             1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUtensorMapDataType dt = dtype == FA_DTYPE_FP16   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                           : dtype == FA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUtensorMapSwizzle sw = swz_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : swz_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                            : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = enc(map, dt, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FA_OK : FA_ERR_TENSOR_MAP;
+}
+
+int validate(const FaFwdArgs* a) {
+  if (!a || a->struct_size != static_cast<int32_t>(sizeof(FaFwdArgs))) return FA_ERR_INVALID_ARG;
+  if (a->batch <= 0 || a->heads <= 0 || a->seqlen <= 0) return FA_ERR_INVALID_ARG;
+  if (a->seqlen > (int64_t{1} << 30) || a->batch * a->heads > (int64_t{1} << 30))
+    return FA_ERR_INVALID_ARG;
+  if (!head_dim_ok(a->head_dim)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  if (a->dtype != FA_DTYPE_FP16 && a->dtype != FA_DTYPE_BF16 && a->dtype != FA_DTYPE_FP32)
+    return FA_ERR_UNSUPPORTED_DTYPE;
+  if (!a->q || !a->k || !a->v || !a->o || !a->lse) return FA_ERR_INVALID_ARG;
+  if (!std::isfinite(a->sm_scale)) return FA_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(a->lse) % 4 != 0) return FA_ERR_MISALIGNED;
+  return FA_OK;
+}
+
+int resolve_tile(const FaFwdArgs* a, FaTileConfig* t) {
+  *t = a->tile;
+  if (t->block_m == 0 && t->block_n == 0) {
+    int rc = fa_fwd_sm100_default_tile(a->head_dim, a->dtype, a->causal, a->seqlen, t);
+    if (rc != FA_OK) return rc;
+    t->num_stages = a->tile.num_stages;
+    t->persistent_ctas = a->tile.persistent_ctas;
+  }
+  if (t->block_m != 128 && t->block_m != 256) return FA_ERR_UNSUPPORTED_TILE;
+  if (t->block_n != 64 && t->block_n != 128) return FA_ERR_UNSUPPORTED_TILE;
+  const fa::KernelInfo ki = info_for(a->head_dim, a->dtype, t->block_n, t->block_m / 128);
+  if (!ki.exists) return FA_ERR_UNSUPPORTED_TILE;
+  const int smax = max_stages_for(ki);
+  if (smax < 2) return FA_ERR_UNSUPPORTED_TILE;
+  if (t->num_stages == 0) t->num_stages = smax;
+  if (t->num_stages < 2 || t->num_stages > smax) return FA_ERR_UNSUPPORTED_TILE;
+  if (t->persistent_ctas < 0) return FA_ERR_UNSUPPORTED_TILE;
+  return FA_OK;
+}
+
+}  // namespace
+
+namespace fa {
+KernelInfo kernel_info(int head_dim, int dtype, int block_n, int qt) {
+  return info_for(head_dim, dtype, block_n, qt);
+}
+}  // namespace fa
+
+extern "C" {
+
+int fa_fwd_sm100_default_tile(int64_t head_dim, int32_t dtype, int32_t causal, int64_t seqlen,
+                              FaTileConfig* cfg) {
+  (void)causal;
+  if (!cfg) return FA_ERR_INVALID_ARG;
+  if (!head_dim_ok(head_dim)) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  if (dtype != FA_DTYPE_FP16 && dtype != FA_DTYPE_BF16 && dtype != FA_DTYPE_FP32)
+    return FA_ERR_UNSUPPORTED_DTYPE;
+  FaTileConfig t{};
+  if (dtype == FA_DTYPE_FP32) {
+    if (head_dim > 128) return FA_ERR_UNSUPPORTED_TILE;
+    t.block_m = 128;
+    t.block_n = 64;
+  } else if (head_dim == 256) {
+    t.block_m = 128;
+    t.block_n = 64;
+  } else {
+    // Two 128-row query tiles share every K/V tile; a single tile for short sequences.
+    t.block_m = seqlen > 128 ? 256 : 128;
+    t.block_n = 128;
+  }
+  t.num_stages = 0;
+  t.persistent_ctas = 0;
+  *cfg = t;
+  return FA_OK;
+}
+
+int fa_fwd_sm100_supported(int64_t head_dim, int32_t dtype, int32_t block_m, int32_t block_n,
+                           int32_t num_stages) {
+  if (!head_dim_ok(head_dim)) return 0;
+  if (block_m != 128 && block_m != 256) return 0;
+  if (block_n != 64 && block_n != 128) return 0;
+  const fa::KernelInfo ki = info_for(head_dim, dtype, block_n, block_m / 128);
+  const int smax = max_stages_for(ki);
+  if (smax < 2) return 0;
+  if (num_stages == 0) return 1;
+  return (num_stages >= 2 && num_stages <= smax) ? 1 : 0;
+}
+
+int fa_fwd_sm100_max_stages(int64_t head_dim, int32_t dtype, int32_t block_m, int32_t block_n) {
+  if (!head_dim_ok(head_dim) || (block_m != 128 && block_m != 256)) return 0;
+  const int s = max_stages_for(info_for(head_dim, dtype, block_n, block_m / 128));
+  return s >= 2 ? s : 0;
+}
+
+int64_t fa_fwd_sm100_grid_size(const FaFwdArgs* a) {
+  if (validate(a) != FA_OK) return -1;
+  FaTileConfig t;
+  if (resolve_tile(a, &t) != FA_OK) return -1;
+  const int64_t nq = (a->seqlen + t.block_m - 1) / t.block_m;
+  return nq * a->batch * a->heads;
+}
+
+int fa_fwd_sm100(const FaFwdArgs* a, void* stream) {
+  int rc = validate(a);
+  if (rc != FA_OK) return rc;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return FA_ERR_DEVICE;
+  }
+  if (!device_ok(dev)) return FA_ERR_DEVICE;
+  FaTileConfig t;
+  rc = resolve_tile(a, &t);
+  if (rc != FA_OK) return rc;
+  const int qt = t.block_m / 128;
+  const fa::KernelInfo ki = info_for(a->head_dim, a->dtype, t.block_n, qt);
+
+  fa::LaunchPlan lp;
+  std::memset(&lp, 0, sizeof(lp));
+  const int64_t B = a->batch, H = a->heads, S = a->seqlen, D = a->head_dim;
+  rc = encode_map(&lp.tmQ, a->q, a->dtype, B, H, S, D, a->q_stride, ki.box_cols, 128, ki.swz_bytes);
+  if (rc == FA_OK)
+    rc = encode_map(&lp.tmK, a->k, a->dtype, B, H, S, D, a->k_stride, ki.box_cols, t.block_n,
+                    ki.swz_bytes);
+  if (rc == FA_OK)
+    rc = encode_map(&lp.tmV, a->v, a->dtype, B, H, S, D, a->v_stride, ki.box_cols, t.block_n,
+                    ki.swz_bytes);
+  if (rc == FA_OK)
+    rc = encode_map(&lp.tmO, a->o, a->dtype, B, H, S, D, a->o_stride, ki.box_cols, 128,
+                    ki.swz_bytes);
+  if (rc != FA_OK) return rc;
+
+  const int64_t nq = (S + t.block_m - 1) / t.block_m;
+  lp.grid = nq * B * H;
+  if (lp.grid > 0x7fffffffLL) return FA_ERR_INVALID_ARG;
+  lp.params.batch = static_cast<int>(B);
+  lp.params.heads = static_cast<int>(H);
+  lp.params.seqlen = static_cast<int>(S);
+  lp.params.n_qblocks = static_cast<int>(nq);
+  lp.params.causal = a->causal ? 1 : 0;
+  lp.params.stages = t.num_stages;
+  lp.params.scale_log2 = a->sm_scale * fa::kLog2e;
+  lp.params.lse = a->lse;
+  lp.params.status = a->dev_status;
+  lp.dtype = a->dtype;
+  lp.block_n = t.block_n;
+  lp.qt = qt;
+  lp.stream = static_cast<cudaStream_t>(stream);
+
+  switch (D) {
+    case 16: return fa::launch_d16(lp);
+    case 32: return fa::launch_d32(lp);
+    case 64: return fa::launch_d64(lp);
+    case 128: return fa::launch_d128(lp);
+    case 256: return fa::launch_d256(lp);
+    default: return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  }
+}
+
+const char* fa_fwd_sm100_status_string(int code) {
+  switch (code) {
+    case FA_OK: return "ok";
+    case FA_ERR_INVALID_ARG: return "invalid argument";
+    case FA_ERR_UNSUPPORTED_HEAD_DIM: return "HEAD_DIM must be one of {16, 32, 64, 128, 256}";
+    case FA_ERR_UNSUPPORTED_DTYPE: return "dtype must be float16, bfloat16 or float32";
+    case FA_ERR_MISALIGNED:
+      return "tensor pointer or stride is not 16-byte aligned (TMA requirement)";
+    case FA_ERR_UNSUPPORTED_TILE: return "tile configuration not available for this head_dim/dtype";
+    case FA_ERR_TENSOR_MAP: return "cuTensorMapEncodeTiled failed";
+    case FA_ERR_LAUNCH: return "kernel launch failed";
+    case FA_ERR_DEVICE: return "current CUDA device is not an sm_100 (B200) part";
+    case FA_ERR_DEVICE_TIMEOUT: return "a pipeline wait in the kernel timed out";
+    default: return "unknown status";
+  }
+}
+
+int fa_fwd_sm100_version(void) { return 1000; }
+
+}  // extern "C"

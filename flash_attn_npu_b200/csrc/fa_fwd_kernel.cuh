@@ -1,0 +1,623 @@
+// FlashAttention forward for B200 (sm_100a): warp-specialised TMA -> tcgen05 -> TMEM pipeline.
+//
+// What it computes (same contract as the reference Triton kernel `_attn_fwd`,
+// flash_attention_forward.py:1036-1111 and its tile body `_attn_fwd_tile`, :872-1033):
+//   O[b,h,i,:]  = sum_j softmax_j(scale * q_i . k_j) v_j      (keys j <= i when causal)
+//   LSE[b,h,i]  = log sum_j exp(scale * q_i . k_j)           (natural log, fp32)
+// The reference keeps a running max m and sum l (`_attn_fwd_inner_loop`, :698-724) and
+// finishes with m += log(l), O = acc / l (:1022-1033).  This kernel keeps the same online
+// softmax but works in base 2 (exp2 with scale*log2(e) folded in), applies the scale to the
+// fp32 logits instead of pre-rounding q (:977-978), masks with -inf rather than -1e6
+// (:694-696), and masks the key tail instead of dropping keys past the last full block (:846-869).
+//
+// CTA shape (one CTA per SM; TMEM and shared memory sized for that):
+//   QT query tiles of 128 rows for one (batch, head); BLOCK_M = 128 * QT.
+//   warp 0        : TMA producer (Q once, then K/V tiles into a ring of `stages` slots)
+//   warp 1        : TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2-3     : idle (keep the softmax warpgroups aligned to TMEM lane quarters)
+//   warps 4+4i..  : softmax warpgroup i (thread r owns query row r of tile i = TMEM lane r)
+// TMEM columns: S_i (fp32 logits, BN cols) at i*BN, then O_i (fp32, D cols) at QT*BN + i*D.
+// P_i (the probabilities, in the input dtype) is written back over the first columns of S_i
+// and consumed from TMEM by the P.V MMA (A operand in tensor memory).
+//
+// Per KV step j the MMA thread issues, for each tile i in order:
+//   O_i (+)= P_i(j) V_j ;  S_i(j+1) = Q_i K_{j+1}^T
+// tcgen05 MMAs from one thread complete in issue order, so when softmax warpgroup i sees
+// S_i(j+1) complete, O_i already holds P_i(j) V_j: the warpgroup can rescale O_i in TMEM
+// before releasing P_i(j+1), with no extra barrier.
+//
+// Rescaling is conditional: the exponent base m only moves when the row max grows by more
+// than RESCALE_LOG2 (p values then stay <= 2^RESCALE_LOG2).  The result is exact because
+// l and O are both accumulated against the same base.
+//
+// Every wait is bounded (FA_WAIT_TIMEOUT_NS); a wait that gives up records
+// FA_ERR_DEVICE_TIMEOUT in *status, raises a CTA-wide abort flag and all roles drain to the
+// teardown, which waits for in-flight copies and MMAs before TMEM is freed.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "sm100_ptx.cuh"
+
+#ifndef FA_WAIT_TIMEOUT_NS
+#define FA_WAIT_TIMEOUT_NS 2000000000ull
+#endif
+
+namespace fa {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float RESCALE_LOG2 = 8.0f;
+constexpr int kMaxStages = 8;
+constexpr int kStatusTimeout = -9;  // FA_ERR_DEVICE_TIMEOUT
+
+struct FaParams {
+  int batch;
+  int heads;
+  int seqlen;
+  int n_qblocks;   // ceil(seqlen / BLOCK_M)
+  int causal;
+  int stages;      // K/V ring depth
+  float scale_log2;
+  float* lse;      // [B, H, S] fp32 contiguous
+  int* status;     // optional
+};
+
+template <typename T>
+struct Elt;
+template <>
+struct Elt<__nv_bfloat16> {
+  static constexpr int kBytes = 2;
+  static constexpr uint32_t kFmt = 1;
+  static constexpr bool kTf32 = false;
+};
+template <>
+struct Elt<__half> {
+  static constexpr int kBytes = 2;
+  static constexpr uint32_t kFmt = 0;
+  static constexpr bool kTf32 = false;
+};
+template <>
+struct Elt<float> {
+  static constexpr int kBytes = 4;
+  static constexpr uint32_t kFmt = 2;
+  static constexpr bool kTf32 = true;
+};
+
+// Compile-time geometry of one kernel instantiation.
+template <typename T, int D, int BN, int QT>
+struct Geo {
+  static constexpr int EB = Elt<T>::kBytes;
+  static constexpr int ROW_BYTES = D * EB;                        // one row of Q/K/V/O
+  static constexpr int SWZ = ROW_BYTES >= 128 ? 128 : ROW_BYTES;  // swizzle span (32/64/128 B)
+  static constexpr int BLK_COLS = SWZ / EB;                       // TMA box inner extent
+  static constexpr int NBLK = ROW_BYTES / SWZ;                    // column blocks per row
+  static constexpr int BM = 128;                                  // rows per query tile
+  static constexpr int Q_BLK_BYTES = BM * SWZ;
+  static constexpr int Q_TILE_BYTES = BM * ROW_BYTES;
+  static constexpr int KV_BLK_BYTES = BN * SWZ;
+  static constexpr int KV_TILE_BYTES = BN * ROW_BYTES;
+  static constexpr int KSTEPS_PER_BLK = SWZ / 32;  // MMA K is always 32 bytes
+  static constexpr int MMA_K = 32 / EB;            // 16 (f16/bf16) or 8 (tf32)
+  static constexpr int P_COLS = BN * EB / 4;       // TMEM columns holding P
+  static constexpr int TMEM_S = 0;
+  static constexpr int TMEM_O = QT * BN;
+  static constexpr int TMEM_USED = QT * (BN + D);
+  static constexpr int TMEM_ALLOC = TMEM_USED <= 32    ? 32
+                                    : TMEM_USED <= 64  ? 64
+                                    : TMEM_USED <= 128 ? 128
+                                    : TMEM_USED <= 256 ? 256
+                                                       : 512;
+  static constexpr int NUM_THREADS = 128 + 128 * QT;
+  static constexpr uint32_t LAYOUT = SWZ == 128 ? 2u : (SWZ == 64 ? 4u : 6u);
+  static constexpr uint32_t IDESC_S = make_idesc(Elt<T>::kFmt, false, 128, BN);
+  static constexpr uint32_t IDESC_O = make_idesc(Elt<T>::kFmt, true, 128, D);
+  // Shared memory: [Q tiles][K/V ring][barriers]; +1024 for base alignment.
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int smem_bytes(int stages) {
+    return 1024 + QT * Q_TILE_BYTES + stages * KV_TILE_BYTES + BAR_BYTES;
+  }
+  static_assert(TMEM_USED <= 512, "TMEM budget exceeded");
+  static_assert(BN == 64 || BN == 128, "BLOCK_N must be 64 or 128");
+  static_assert(QT == 1 || QT == 2, "1 or 2 query tiles per CTA");
+  static_assert(D % 16 == 0 && D >= 16 && D <= 256, "head_dim");
+  static_assert(ROW_BYTES % SWZ == 0, "row must be whole swizzle spans");
+  static_assert(Q_BLK_BYTES % 1024 == 0 && KV_BLK_BYTES % 1024 == 0, "1 KiB tile alignment");
+};
+
+// Physical byte offset of logical byte `off` inside a TMA-swizzled region with span SWZ.
+template <int SWZ>
+__device__ __forceinline__ uint32_t swizzle(uint32_t off) {
+  constexpr uint32_t mask = SWZ / 16 - 1;
+  return off ^ (((off >> 7) & mask) << 4);
+}
+
+struct Shared {
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
+  uint64_t q_full;
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_full[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  volatile uint32_t abort_flag;
+};
+static_assert(sizeof(Shared) <= 256, "barrier block");
+
+// Bounded mbarrier wait.  Returns false on timeout or if another role already aborted.
+__device__ __forceinline__ bool wait_bar(Shared* sh, uint32_t bar, uint32_t parity, int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (sh->abort_flag) return false;
+    if (globaltimer_ns() - t0 > FA_WAIT_TIMEOUT_NS) {
+      sh->abort_flag = 1u;
+      if (status) atomicCAS(status, 0, kStatusTimeout);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, __nv_bfloat16*) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, __half*) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// --------------------------------------------------------------------------------------
+template <typename T, int D, int BN, int QT>
+__global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
+    fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
+                        const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV,
+                        const __grid_constant__ CUtensorMap tmO, const FaParams p) {
+  using G = Geo<T, D, BN, QT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* q_smem = smem;
+  uint8_t* kv_smem = smem + QT * G::Q_TILE_BYTES;
+  Shared* sh = reinterpret_cast<Shared*>(kv_smem + p.stages * G::KV_TILE_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int stages = p.stages;
+
+  // ---- tile coordinates (causal: longest q-blocks first; non-causal: q-blocks of one head
+  //      adjacent so K/V stay in L2 -- the reference's two orders, :915-922)
+  const int bh_count = p.batch * p.heads;
+  int qblk, bh;
+  if (p.causal) {
+    qblk = p.n_qblocks - 1 - static_cast<int>(blockIdx.x / bh_count);
+    bh = static_cast<int>(blockIdx.x % bh_count);
+  } else {
+    bh = static_cast<int>(blockIdx.x / p.n_qblocks);
+    qblk = static_cast<int>(blockIdx.x % p.n_qblocks);
+  }
+  const int bi = bh / p.heads;
+  const int hi = bh % p.heads;
+  const int q0 = qblk * (G::BM * QT);
+
+  // KV steps needed by each query tile (0 = tile lies entirely past the sequence end).
+  int n_kv[QT];
+  int n_max = 0;
+#pragma unroll
+  for (int i = 0; i < QT; ++i) {
+    const int row0 = q0 + G::BM * i;
+    if (row0 >= p.seqlen) {
+      n_kv[i] = 0;
+    } else {
+      const int kv_end = p.causal ? min(p.seqlen, row0 + G::BM) : p.seqlen;
+      n_kv[i] = (kv_end + BN - 1) / BN;
+    }
+    n_max = max(n_max, n_kv[i]);
+  }
+
+  // ---- setup
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(smem_u32(&sh->full[s]), 1);
+      mbar_init(smem_u32(&sh->empty[s]), 1);
+    }
+    mbar_init(smem_u32(&sh->q_full), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&sh->s_full[i]), 1);
+      mbar_init(smem_u32(&sh->p_full[i]), 128);
+      mbar_init(smem_u32(&sh->o_full[i]), 1);
+    }
+    mbar_init(smem_u32(&sh->mma_done), 1);
+    sh->abort_flag = 0u;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+    prefetch_tmap(&tmO);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&sh->tmem_base), G::TMEM_ALLOC);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+
+  if (warp == 0) {
+    // ================================================================ TMA producer
+    if (lane == 0) {
+      int issued = 0;  // K/V ring loads issued
+      bool q_issued = false;
+      bool ok = true;
+      if (n_max > 0) {
+        uint32_t qbytes = 0;
+#pragma unroll
+        for (int i = 0; i < QT; ++i)
+          if (n_kv[i] > 0) qbytes += G::Q_TILE_BYTES;
+        const uint32_t qbar = smem_u32(&sh->q_full);
+        mbar_arrive_expect_tx(qbar, qbytes);
+#pragma unroll
+        for (int i = 0; i < QT; ++i) {
+          if (n_kv[i] == 0) continue;
+#pragma unroll
+          for (int c = 0; c < G::NBLK; ++c)
+            tma_load_4d(smem_u32(q_smem + i * G::Q_TILE_BYTES + c * G::Q_BLK_BYTES), &tmQ, qbar,
+                        c * G::BLK_COLS, q0 + G::BM * i, hi, bi);
+        }
+        q_issued = true;
+        int slot = 0;
+        uint32_t phase = 0;
+        for (int j = 0; j < n_max && ok; ++j) {
+#pragma unroll
+          for (int kv = 0; kv < 2; ++kv) {
+            if (!wait_bar(sh, smem_u32(&sh->empty[slot]), phase ^ 1u, p.status)) {
+              ok = false;
+              break;
+            }
+            const uint32_t fbar = smem_u32(&sh->full[slot]);
+            mbar_arrive_expect_tx(fbar, G::KV_TILE_BYTES);
+            const CUtensorMap* map = kv == 0 ? &tmK : &tmV;
+            uint8_t* dst = kv_smem + slot * G::KV_TILE_BYTES;
+#pragma unroll
+            for (int c = 0; c < G::NBLK; ++c)
+              tma_load_4d(smem_u32(dst + c * G::KV_BLK_BYTES), map, fbar, c * G::BLK_COLS, j * BN,
+                          hi, bi);
+            ++issued;
+            if (++slot == stages) {
+              slot = 0;
+              phase ^= 1u;
+            }
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: every load issued must land before the CTA's shared memory goes away.
+        if (q_issued) wait_bar(sh, smem_u32(&sh->q_full), 0, nullptr);
+        const int outstanding = min(issued, stages);
+        for (int t = 0; t < outstanding; ++t) {
+          const int idx = issued - 1 - t;
+          const uint32_t bar = smem_u32(&sh->full[idx % stages]);
+          const uint32_t par = static_cast<uint32_t>((idx / stages) & 1);
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(bar, par) && globaltimer_ns() - t0 < FA_WAIT_TIMEOUT_NS) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ================================================================ MMA issuer
+    if (lane == 0 && n_max > 0) {
+      bool ok = wait_bar(sh, smem_u32(&sh->q_full), 0, p.status);
+      tc_fence_after();
+      // ring position of K_j is 2j, of V_j is 2j+1
+      auto slot_of = [&](int pos) { return pos % stages; };
+      auto par_of = [&](int pos) { return static_cast<uint32_t>((pos / stages) & 1); };
+      const uint32_t q_base = smem_u32(q_smem);
+      const uint32_t kv_base = smem_u32(kv_smem);
+
+      // S_i = Q_i K^T : A = Q tile (K-major), B = K tile (K-major), both SWZ-swizzled.
+      auto issue_s = [&](int i, int kslot) {
+        const uint32_t a0 = q_base + i * G::Q_TILE_BYTES;
+        const uint32_t b0 = kv_base + kslot * G::KV_TILE_BYTES;
+        const uint32_t d = tmem + G::TMEM_S + i * BN;
+#pragma unroll
+        for (int c = 0; c < G::NBLK; ++c) {
+#pragma unroll
+          for (int kk = 0; kk < G::KSTEPS_PER_BLK; ++kk) {
+            const uint64_t ad = make_smem_desc(a0 + c * G::Q_BLK_BYTES + kk * 32, 16, 8 * G::SWZ,
+                                               G::LAYOUT);
+            const uint64_t bd = make_smem_desc(b0 + c * G::KV_BLK_BYTES + kk * 32, 16, 8 * G::SWZ,
+                                               G::LAYOUT);
+            const uint32_t acc = (c | kk) ? 1u : 0u;
+            if constexpr (Elt<T>::kTf32)
+              mma_tf32_ss(d, ad, bd, G::IDESC_S, acc);
+            else
+              mma_f16_ss(d, ad, bd, G::IDESC_S, acc);
+          }
+        }
+      };
+      // O_i (+)= P_i V : A = P_i in TMEM, B = V tile (MN-major: rows = keys, cols = head dim).
+      auto issue_pv = [&](int i, int vslot, bool accumulate) {
+        const uint32_t b0 = kv_base + vslot * G::KV_TILE_BYTES;
+        const uint32_t d = tmem + G::TMEM_O + i * D;
+        const uint32_t a = tmem + G::TMEM_S + i * BN;
+#pragma unroll
+        for (int kk = 0; kk < BN / G::MMA_K; ++kk) {
+          // MMA_K keys = MMA_K rows of V = MMA_K/8 eight-row groups of SWZ bytes each
+          const uint64_t bd = make_smem_desc(b0 + kk * G::MMA_K * G::SWZ, G::KV_BLK_BYTES,
+                                             8 * G::SWZ, G::LAYOUT);
+          const uint32_t acc = (accumulate || kk > 0) ? 1u : 0u;
+          // each TMEM column holds 4 bytes of P: MMA_K elements = MMA_K*EB/4 columns
+          const uint32_t acol = static_cast<uint32_t>(kk * G::MMA_K * G::EB / 4);
+          if constexpr (Elt<T>::kTf32)
+            mma_tf32_ts(d, a + acol, bd, G::IDESC_O, acc);
+          else
+            mma_f16_ts(d, a + acol, bd, G::IDESC_O, acc);
+        }
+      };
+
+      if (ok) ok = wait_bar(sh, smem_u32(&sh->full[slot_of(0)]), par_of(0), p.status);
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int i = 0; i < QT; ++i) {
+          if (n_kv[i] == 0) continue;
+          issue_s(i, slot_of(0));
+          mma_commit(smem_u32(&sh->s_full[i]));
+        }
+        mma_commit(smem_u32(&sh->empty[slot_of(0)]));
+      }
+      for (int j = 0; j < n_max && ok; ++j) {
+        const int vpos = 2 * j + 1;
+        const int kpos = 2 * j + 2;
+        ok = wait_bar(sh, smem_u32(&sh->full[slot_of(vpos)]), par_of(vpos), p.status);
+        if (!ok) break;
+        bool k_ready = false;
+#pragma unroll
+        for (int i = 0; i < QT; ++i) {
+          if (j >= n_kv[i]) continue;
+          ok = wait_bar(sh, smem_u32(&sh->p_full[i]), static_cast<uint32_t>(j & 1), p.status);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(i, slot_of(vpos), j > 0);
+          if (j == n_kv[i] - 1) mma_commit(smem_u32(&sh->o_full[i]));
+          if (j + 1 < n_kv[i]) {
+            if (!k_ready) {
+              ok = wait_bar(sh, smem_u32(&sh->full[slot_of(kpos)]), par_of(kpos), p.status);
+              if (!ok) break;
+              tc_fence_after();
+              k_ready = true;
+            }
+            issue_s(i, slot_of(kpos));
+            mma_commit(smem_u32(&sh->s_full[i]));
+          }
+        }
+        if (!ok) break;
+        mma_commit(smem_u32(&sh->empty[slot_of(vpos)]));
+        if (k_ready) mma_commit(smem_u32(&sh->empty[slot_of(kpos)]));
+      }
+      // All MMAs issued by this thread must finish before TMEM is released.
+      mma_commit(smem_u32(&sh->mma_done));
+      {
+        const uint32_t bar = smem_u32(&sh->mma_done);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(bar, 0) && globaltimer_ns() - t0 < FA_WAIT_TIMEOUT_NS) {
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ================================================================ softmax warpgroups
+    const int i = (warp - 4) >> 2;  // query tile
+    const int wq = warp & 3;        // TMEM lane quarter
+    const int r = wq * 32 + lane;   // row within the tile
+    const int row = q0 + G::BM * i + r;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS = tmem + lane_off + G::TMEM_S + i * BN;
+    const uint32_t tO = tmem + lane_off + G::TMEM_O + i * D;
+    const float sl2 = p.scale_log2;
+    const bool use_max = sl2 >= 0.f;
+    bool ok = true;
+    float m_used = -INFINITY;  // exponent base, log2 units
+    float l = 0.f;
+    const int nk = (QT == 1 || i == 0) ? n_kv[0] : n_kv[QT - 1];
+
+    for (int j = 0; j < nk; ++j) {
+      ok = wait_bar(sh, smem_u32(&sh->s_full[i]), static_cast<uint32_t>(j & 1), p.status);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, reinterpret_cast<uint32_t*>(s) + c * 32);
+      tmem_wait_ld();
+
+      const int kv0 = j * BN;
+      const bool tail = kv0 + BN > p.seqlen;
+      const bool diag = p.causal && (kv0 + BN - 1 > q0 + G::BM * i);
+      int lim = BN;  // columns >= lim are masked for this row
+      if (tail || diag) {
+        lim = p.seqlen - kv0;
+        if (p.causal) lim = min(lim, row - kv0 + 1);
+        lim = max(0, min(lim, BN));
+      }
+      const bool masked = tail || diag;
+      const float fill = use_max ? -INFINITY : INFINITY;
+
+      // row extreme (max for scale >= 0, min for scale < 0), 8 independent chains
+      float e8[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) e8[t] = fill;
+      if (masked) {
+#pragma unroll
+        for (int k = 0; k < BN; ++k) {
+          const float v = (k < lim) ? s[k] : fill;
+          e8[k & 7] = use_max ? fmaxf(e8[k & 7], v) : fminf(e8[k & 7], v);
+        }
+      } else if (use_max) {
+#pragma unroll
+        for (int k = 0; k < BN; ++k) e8[k & 7] = fmaxf(e8[k & 7], s[k]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < BN; ++k) e8[k & 7] = fminf(e8[k & 7], s[k]);
+      }
+      float ext = e8[0];
+#pragma unroll
+      for (int t = 1; t < 8; ++t) ext = use_max ? fmaxf(ext, e8[t]) : fminf(ext, e8[t]);
+
+      const float m_tile = ext * sl2;                // NaN only when a row is fully masked and scale == 0
+      const float m_new = fmaxf(m_used, m_tile);     // fmaxf drops a NaN operand
+      const bool need = m_new > m_used + RESCALE_LOG2;
+      float alpha = 1.f;
+      if (need) {
+        alpha = ex2_approx(m_used - m_new);  // m_used = -inf gives 0
+        l *= alpha;
+        m_used = m_new;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O_i holds sum over steps < j (S_i(j) completion implies P_i(j-1) V_{j-1} done).
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
+          tmem_st32(tO + c * 32, o);
+        }
+        if constexpr (D % 32 == 16) {
+          uint32_t o[16];
+          tmem_ld16(tO + (D / 32) * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int t = 0; t < 16; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
+          tmem_st16(tO + (D / 32) * 32, o);
+        }
+      }
+
+      // p = 2^(s*scale_log2 - m_used); masked columns -> 0
+      const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+      float l8[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) l8[t] = 0.f;
+      if (masked) {
+#pragma unroll
+        for (int k = 0; k < BN; ++k) {
+          const float x = (k < lim) ? fmaf(s[k], sl2, neg_m) : -INFINITY;
+          s[k] = ex2_approx(x);
+          l8[k & 7] += s[k];
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < BN; ++k) {
+          s[k] = ex2_approx(fmaf(s[k], sl2, neg_m));
+          l8[k & 7] += s[k];
+        }
+      }
+      l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+
+      // P back into TMEM (over the first P_COLS columns of S_i)
+      if constexpr (Elt<T>::kTf32) {
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+          tmem_st32(tS + c * 32, reinterpret_cast<const uint32_t*>(s) + c * 32);
+      } else {
+        uint32_t pk[BN / 2];
+#pragma unroll
+        for (int k = 0; k < BN / 2; ++k) pk[k] = pack2(s[2 * k], s[2 * k + 1], static_cast<T*>(nullptr));
+#pragma unroll
+        for (int c = 0; c < BN / 64; ++c) tmem_st32(tS + c * 32, pk + c * 32);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&sh->p_full[i]));
+    }
+
+    // ---------------------------------------------------------------- epilogue
+    bool have_out = false;
+    if (ok && nk > 0) {
+      ok = wait_bar(sh, smem_u32(&sh->o_full[i]), 0, p.status);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        have_out = true;
+        const float inv_l = 1.f / l;
+        // Stage the O tile in this tile's Q buffer (every S MMA has completed).
+        uint8_t* stage = q_smem + i * G::Q_TILE_BYTES;
+        constexpr int CH = (D % 32 == 0) ? 32 : 16;
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += CH) {
+          uint32_t o[32];
+          if constexpr (CH == 32)
+            tmem_ld32(tO + c0, o);
+          else
+            tmem_ld16(tO + c0, o);
+          tmem_wait_ld();
+          // CH columns -> CH*EB bytes -> CH*EB/16 chunks of 16 bytes
+          const int blk = (c0 * G::EB) / G::SWZ;
+          const int inblk = (c0 * G::EB) % G::SWZ;
+          uint8_t* base = stage + blk * G::Q_BLK_BYTES;
+          if constexpr (Elt<T>::kTf32) {
+#pragma unroll
+            for (int q = 0; q < CH / 4; ++q) {
+              uint4 w;
+              w.x = __float_as_uint(__uint_as_float(o[4 * q + 0]) * inv_l);
+              w.y = __float_as_uint(__uint_as_float(o[4 * q + 1]) * inv_l);
+              w.z = __float_as_uint(__uint_as_float(o[4 * q + 2]) * inv_l);
+              w.w = __float_as_uint(__uint_as_float(o[4 * q + 3]) * inv_l);
+              const uint32_t off = swizzle<G::SWZ>(r * G::SWZ + inblk + q * 16);
+              *reinterpret_cast<uint4*>(base + off) = w;
+            }
+          } else {
+#pragma unroll
+            for (int q = 0; q < CH / 8; ++q) {
+              uint4 w;
+              w.x = pack2(__uint_as_float(o[8 * q + 0]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l, static_cast<T*>(nullptr));
+              w.y = pack2(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l, static_cast<T*>(nullptr));
+              w.z = pack2(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l, static_cast<T*>(nullptr));
+              w.w = pack2(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l, static_cast<T*>(nullptr));
+              const uint32_t off = swizzle<G::SWZ>(r * G::SWZ + inblk + q * 16);
+              *reinterpret_cast<uint4*>(base + off) = w;
+            }
+          }
+        }
+        if (row < p.seqlen) {
+          const float lse = (m_used + log2f(l)) * kLn2;
+          p.lse[(static_cast<int64_t>(bh) * p.seqlen) + row] = lse;
+        }
+        fence_proxy_async_smem();
+      }
+    }
+    // All 128 threads of the warpgroup reach this barrier exactly once.
+    named_barrier_sync(1 + i, 128);
+    if (have_out && r == 0) {
+      uint8_t* stage = q_smem + i * G::Q_TILE_BYTES;
+#pragma unroll
+      for (int c = 0; c < G::NBLK; ++c)
+        tma_store_4d(&tmO, smem_u32(stage + c * G::Q_BLK_BYTES), c * G::BLK_COLS,
+                     q0 + G::BM * i, hi, bi);
+      bulk_commit_group();
+      bulk_wait_group_read0();
+    }
+  }
+
+  // ---- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, G::TMEM_ALLOC);
+  }
+}
+
+}  // namespace fa

@@ -1,0 +1,71 @@
+// Internal launch plan shared by the C-ABI front end (fa_fwd_api.cu) and the per-head-dim
+// translation units (fa_fwd_d*.cu) that hold the kernel instantiations.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "fa_fwd_kernel.cuh"
+
+namespace fa {
+
+struct LaunchPlan {
+  CUtensorMap tmQ, tmK, tmV, tmO;
+  FaParams params;
+  int dtype;    // FaDtype
+  int block_n;  // 64 / 128
+  int qt;       // query tiles per CTA (block_m / 128)
+  int64_t grid;
+  cudaStream_t stream;
+};
+
+// Kernel geometry facts the host needs before launching (shared-memory size, TMA boxes).
+struct KernelInfo {
+  bool exists;
+  int swz_bytes;      // swizzle span of Q/K/V/O tiles
+  int box_cols;       // TMA box inner extent (elements)
+  int q_tile_bytes;   // one 128-row query tile
+  int kv_tile_bytes;  // one BLOCK_N-row K or V tile
+  int threads;
+  int smem_fixed;     // bytes besides the K/V ring
+};
+
+KernelInfo kernel_info(int head_dim, int dtype, int block_n, int qt);
+KernelInfo info_d16(int dtype, int block_n, int qt);
+KernelInfo info_d32(int dtype, int block_n, int qt);
+KernelInfo info_d64(int dtype, int block_n, int qt);
+KernelInfo info_d128(int dtype, int block_n, int qt);
+KernelInfo info_d256(int dtype, int block_n, int qt);
+
+int launch_d16(const LaunchPlan& lp);
+int launch_d32(const LaunchPlan& lp);
+int launch_d64(const LaunchPlan& lp);
+int launch_d128(const LaunchPlan& lp);
+int launch_d256(const LaunchPlan& lp);
+
+// Launch one instantiation; returns 0 or FA_ERR_LAUNCH (-7) / FA_ERR_UNSUPPORTED_TILE (-5).
+template <typename T, int D, int BN, int QT>
+int launch_kernel(const LaunchPlan& lp) {
+  using G = Geo<T, D, BN, QT>;
+  auto kern = fa_fwd_sm100_kernel<T, D, BN, QT>;
+  const int smem = G::smem_bytes(lp.params.stages);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess) {
+    (void)cudaGetLastError();
+    return -7;
+  }
+  kern<<<dim3(static_cast<unsigned>(lp.grid)), dim3(G::NUM_THREADS), smem, lp.stream>>>(
+      lp.tmQ, lp.tmK, lp.tmV, lp.tmO, lp.params);
+  return cudaGetLastError() == cudaSuccess ? 0 : -7;
+}
+
+template <typename T, int D, int BN, int QT>
+constexpr KernelInfo info_of() {
+  using G = Geo<T, D, BN, QT>;
+  return KernelInfo{true,           G::SWZ,         G::BLK_COLS,
+                    G::Q_TILE_BYTES, G::KV_TILE_BYTES, G::NUM_THREADS,
+                    G::smem_bytes(0)};
+}
+
+}  // namespace fa

@@ -1,0 +1,131 @@
+"""Torch-facing forward op: validate, allocate, launch the sm_100a kernel through the C ABI.
+
+This is the host half of the reference's `_launch_kernel` (flash_attention_forward.py:1130-1194):
+  - `_validate_inputs` rules (:1114-1122) raise ValueError,
+  - `out = torch.empty_like(q)` and an fp32 `lse` of shape [Z, H, N_CTX] (:1135-1136),
+  - asynchronous launch on the current stream.
+The Ascend-only pieces (UB accumulator workspace, lazy-softmax switch) have no counterpart:
+the B200 kernel keeps the accumulator in TMEM and always uses the stable online softmax.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native
+
+HEAD_DIMS = (16, 32, 64, 128, 256)
+
+_DTYPE_CODES = {
+    torch.float16: _native.FA_DTYPE_FP16,
+    torch.bfloat16: _native.FA_DTYPE_BF16,
+    torch.float32: _native.FA_DTYPE_FP32,
+}
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODES[dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {dtype}; expected float16, bfloat16 or float32")
+
+
+def validate_inputs(q, k, v) -> None:
+    """Reference `_validate_inputs` (flash_attention_forward.py:1114-1122) plus the CUDA rules."""
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise ValueError("q, k, v must all be 4D tensors shaped [Z, H, N_CTX, HEAD_DIM]")
+    if q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("q, k, v must have the same shape")
+    if q.device != k.device or q.device != v.device:
+        raise ValueError("q, k, v must be on the same device")
+    if q.shape[-1] not in set(HEAD_DIMS):
+        raise ValueError("HEAD_DIM must be one of {16, 32, 64, 128, 256}")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError("q, k, v must have the same dtype")
+    dtype_code(q.dtype)
+    if q.device.type != "cuda":
+        raise ValueError(f"q, k, v must be CUDA tensors on an sm_100 device (got {q.device})")
+
+
+def _tma_ok(t: torch.Tensor) -> bool:
+    """True if `t` can be described by a TMA tensor map as-is (16-byte rule, unit inner stride)."""
+    if t.stride(-1) != 1:
+        return False
+    eb = t.element_size()
+    if t.data_ptr() % 16 != 0:
+        return False
+    for dim in range(3):
+        if t.shape[dim] > 1 and (t.stride(dim) * eb) % 16 != 0:
+            return False
+    return True
+
+
+def _tma_view(t: torch.Tensor) -> torch.Tensor:
+    return t if _tma_ok(t) else t.contiguous()
+
+
+def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_scale: float, *,
+            block_m: int = 0, block_n: int = 0, num_stages: int = 0, persistent_ctas: int = 0,
+            out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
+            status: torch.Tensor | None = None):
+    """Run attention forward on the B200 kernel; returns (out, lse).
+
+    `block_m/block_n/num_stages/persistent_ctas` = 0 picks the library default.  `out` and
+    `lse` may be preallocated (same shape/dtype rules as the freshly allocated ones).
+    `status`, if given, is a device int32 tensor of one element that must be zero; a pipeline
+    timeout inside the kernel writes a negative code there.
+    """
+    validate_inputs(q, k, v)
+    z, h, n_ctx, head_dim = q.shape
+    code = dtype_code(q.dtype)
+    qv, kv, vv = _tma_view(q), _tma_view(k), _tma_view(v)
+    if out is None:
+        out = torch.empty_like(qv)
+        if not _tma_ok(out):
+            out = torch.empty(qv.shape, dtype=q.dtype, device=q.device)
+    else:
+        if out.shape != q.shape or out.dtype != q.dtype or out.device != q.device:
+            raise ValueError("out must match q in shape, dtype and device")
+        if not _tma_ok(out):
+            raise ValueError("out must have unit inner stride and 16-byte aligned strides")
+    if lse is None:
+        lse = torch.empty((z, h, n_ctx), device=q.device, dtype=torch.float32)
+    elif (lse.shape != (z, h, n_ctx) or lse.dtype != torch.float32 or not lse.is_contiguous()
+          or lse.device != q.device):
+        raise ValueError("lse must be a contiguous float32 tensor of shape [Z, H, N_CTX]")
+    if out.numel() == 0:
+        return out, lse
+    if status is not None and (status.dtype != torch.int32 or status.device != q.device):
+        raise ValueError("status must be an int32 tensor on the same device")
+
+    args = _native.make_args(
+        q_ptr=qv.data_ptr(), k_ptr=kv.data_ptr(), v_ptr=vv.data_ptr(), o_ptr=out.data_ptr(),
+        lse_ptr=lse.data_ptr(), batch=z, heads=h, seqlen=n_ctx, head_dim=head_dim,
+        q_stride=qv.stride()[:3], k_stride=kv.stride()[:3], v_stride=vv.stride()[:3],
+        o_stride=out.stride()[:3], dtype_code=code, causal=causal, sm_scale=sm_scale,
+        block_m=block_m, block_n=block_n, num_stages=num_stages,
+        persistent_ctas=persistent_ctas,
+        status_ptr=(status.data_ptr() if status is not None else None))
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        try:
+            _native.launch(args, stream)
+        except _native.NativeError as exc:
+            if exc.code in (_native.FA_ERR_UNSUPPORTED_HEAD_DIM, _native.FA_ERR_UNSUPPORTED_DTYPE,
+                            _native.FA_ERR_UNSUPPORTED_TILE, _native.FA_ERR_INVALID_ARG,
+                            _native.FA_ERR_MISALIGNED):
+                raise ValueError(str(exc)) from None
+            raise
+    return out, lse
+
+
+def grid_size(z: int, h: int, n_ctx: int, head_dim: int, dtype: torch.dtype, causal: bool,
+              block_m: int = 0, block_n: int = 0) -> int:
+    """CTAs one launch uses (no device needed)."""
+    args = _native.make_args(
+        q_ptr=16, k_ptr=16, v_ptr=16, o_ptr=16, lse_ptr=16, batch=z, heads=h, seqlen=n_ctx,
+        head_dim=head_dim, q_stride=(h * n_ctx * head_dim, n_ctx * head_dim, head_dim),
+        k_stride=(h * n_ctx * head_dim, n_ctx * head_dim, head_dim),
+        v_stride=(h * n_ctx * head_dim, n_ctx * head_dim, head_dim),
+        o_stride=(h * n_ctx * head_dim, n_ctx * head_dim, head_dim), dtype_code=dtype_code(dtype),
+        causal=causal, sm_scale=1.0, block_m=block_m, block_n=block_n)
+    return _native.grid_size(args)
