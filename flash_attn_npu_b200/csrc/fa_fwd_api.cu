@@ -79,7 +79,8 @@ int max_stages_for(const fa::KernelInfo& ki) {
 
 // Encode a 4-D tiled map over a [B, H, S, D] tensor with dims listed innermost first.
 int encode_map(CUtensorMap* map, const void* ptr, int dtype, int64_t B, int64_t H, int64_t S,
-               int64_t D, const int64_t st[3], int box_cols, int box_rows, int swz_bytes) {
+               int64_t D, const int64_t st[3], int box_cols, int box_rows, int swz_bytes,
+               bool atom32 = false) {
   const int eb = elt_bytes(dtype);
   if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return FA_ERR_MISALIGNED;
   // element strides -> byte strides for (seq, head, batch); size-1 dims get a harmless value
@@ -101,7 +102,8 @@ int encode_map(CUtensorMap* map, const void* ptr, int dtype, int64_t B, int64_t 
   CUtensorMapDataType dt = dtype == FA_DTYPE_FP16   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                            : dtype == FA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-  CUtensorMapSwizzle sw = swz_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+  CUtensorMapSwizzle sw = atom32             ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                          : swz_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                           : swz_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                             : CU_TENSOR_MAP_SWIZZLE_32B;
   CUresult r = enc(map, dt, 4, const_cast<void*>(ptr), dims, strides, box, estr,
@@ -163,7 +165,7 @@ int fa_fwd_sm100_default_tile(int64_t head_dim, int32_t dtype, int32_t causal, i
     return FA_ERR_UNSUPPORTED_DTYPE;
   FaTileConfig t{};
   if (dtype == FA_DTYPE_FP32) {
-    if (head_dim > 128) return FA_ERR_UNSUPPORTED_TILE;
+    if (head_dim > 128 || head_dim < 32) return FA_ERR_UNSUPPORTED_TILE;
     t.block_m = 128;
     t.block_n = 64;
   } else if (head_dim == 256) {
@@ -230,7 +232,7 @@ int fa_fwd_sm100(const FaFwdArgs* a, void* stream) {
                     ki.swz_bytes);
   if (rc == FA_OK)
     rc = encode_map(&lp.tmV, a->v, a->dtype, B, H, S, D, a->v_stride, ki.box_cols, t.block_n,
-                    ki.swz_bytes);
+                    ki.swz_bytes, /*atom32=*/a->dtype == FA_DTYPE_FP32);
   if (rc == FA_OK)
     rc = encode_map(&lp.tmO, a->o, a->dtype, B, H, S, D, a->o_stride, ki.box_cols, 128,
                     ki.swz_bytes);

@@ -4,8 +4,9 @@
 // Instantiated tiles (block_m = 128 * QT, block_n = BN):
 //   fp16 / bf16, D <= 128 : (BN, QT) in {(128,2), (64,2), (128,1), (64,1)}
 //   fp16 / bf16, D == 256 : (128,1), (64,1)          (two tiles would need 640 TMEM columns)
-//   fp32 (tf32 MMA), D <= 64  : (128,1), (64,1), (64,2)
-//   fp32 (tf32 MMA), D == 128 : (128,1), (64,1)
+//   fp32 (tf32 MMA), D in {32, 64} : (128,1), (64,1), (64,2)
+//   fp32 (tf32 MMA), D == 128       : (128,1), (64,1)
+//   fp32, D == 16: none (tf32 MN-major V needs 128-byte rows)
 //   fp32, D == 256: none (a 128-row fp32 query tile plus two K/V stages exceeds 227 KiB)
 #pragma once
 
@@ -65,7 +66,7 @@ int FA_CAT(launch_d, FA_HEAD_DIM)(const LaunchPlan& lp) {
     case 1:
       return dispatch_tile<__nv_bfloat16>(lp);
     case 2:
-#if FA_HEAD_DIM <= 128
+#if FA_HEAD_DIM <= 128 && FA_HEAD_DIM >= 32
       return dispatch_tile<float>(lp);
 #else
       return -5;
@@ -82,7 +83,7 @@ KernelInfo FA_CAT(info_d, FA_HEAD_DIM)(int dtype, int block_n, int qt) {
     case 1:
       return info_tile<__nv_bfloat16>(block_n, qt);
     case 2:
-#if FA_HEAD_DIM <= 128
+#if FA_HEAD_DIM <= 128 && FA_HEAD_DIM >= 32
       return info_tile<float>(block_n, qt);
 #else
       return KernelInfo{false, 0, 0, 0, 0, 0, 0};

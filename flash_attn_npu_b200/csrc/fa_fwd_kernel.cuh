@@ -113,6 +113,10 @@ struct Geo {
                                                        : 512;
   static constexpr int NUM_THREADS = 128 + 128 * QT;
   static constexpr uint32_t LAYOUT = SWZ == 128 ? 2u : (SWZ == 64 ? 4u : 6u);
+  // V is the MN-major operand of P.V.  For tf32 that operand needs the 32-byte-atom 128B
+  // swizzle (descriptor code 1, 4-row K groups; TMA CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B).
+  static constexpr uint32_t V_LAYOUT = Elt<T>::kTf32 ? 1u : LAYOUT;
+  static constexpr int V_SBO = Elt<T>::kTf32 ? 4 * SWZ : 8 * SWZ;
   static constexpr uint32_t IDESC_S = make_idesc(Elt<T>::kFmt, false, 128, BN);
   static constexpr uint32_t IDESC_O = make_idesc(Elt<T>::kFmt, true, 128, D);
   // Shared memory: [Q tiles][K/V ring][barriers]; +1024 for base alignment.
@@ -125,6 +129,7 @@ struct Geo {
   static_assert(QT == 1 || QT == 2, "1 or 2 query tiles per CTA");
   static_assert(D % 16 == 0 && D >= 16 && D <= 256, "head_dim");
   static_assert(ROW_BYTES % SWZ == 0, "row must be whole swizzle spans");
+  static_assert(!Elt<T>::kTf32 || SWZ == 128, "tf32 needs rows of >= 128 bytes (head_dim >= 32)");
   static_assert(Q_BLK_BYTES % 1024 == 0 && KV_BLK_BYTES % 1024 == 0, "1 KiB tile alignment");
 };
 
@@ -356,7 +361,7 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
         for (int kk = 0; kk < BN / G::MMA_K; ++kk) {
           // MMA_K keys = MMA_K rows of V = MMA_K/8 eight-row groups of SWZ bytes each
           const uint64_t bd = make_smem_desc(b0 + kk * G::MMA_K * G::SWZ, G::KV_BLK_BYTES,
-                                             8 * G::SWZ, G::LAYOUT);
+                                             G::V_SBO, G::V_LAYOUT);
           const uint32_t acc = (accumulate || kk > 0) ? 1u : 0u;
           // each TMEM column holds 4 bytes of P: MMA_K elements = MMA_K*EB/4 columns
           const uint32_t acol = static_cast<uint32_t>(kk * G::MMA_K * G::EB / 4);

@@ -74,7 +74,7 @@ def geometry(head_dim: int, dtype, cfg: TileConfig) -> dict | None:
     if tmem > TMEM_COLUMNS:
         return None
     if dtype == torch.float32:
-        if head_dim > 128:
+        if head_dim > 128 or head_dim < 32:
             return None
         if qt == 2 and (head_dim > 64 or cfg.block_n != 64):
             return None
