@@ -346,7 +346,7 @@ def run_ours(args, cfg, world, rank, local):
                 worst_l = max(worst_l, (lse_all[s, 0] - rl).abs().max().item())
             verify = {"slices": picks, "max_abs": worst_o, "mean_abs": worst_m,
                       "lse_max_abs": worst_l,
-                      "ok": worst_o <= 2e-2 and worst_m <= 2e-3 and worst_l <= 1e-4 + 1e-6 * 300,
+                      "ok": worst_o <= 2e-2 and worst_m <= 2e-3 and worst_l <= 1e-4,
                       "gathered_with": "nccl p2p" if dist is not None else "local"}
 
     # ---- CPU baseline (rank 0, N = 1 only)

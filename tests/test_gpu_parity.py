@@ -23,15 +23,24 @@ pytestmark = pytest.mark.gpu
 MAX_ABS = 2e-2
 MEAN_ABS = 2e-3
 LSE_ABS = 1e-4
+# LSE bar: 1e-4 absolute plus 2e-6 * |lse|.  For the usual |lse| < 20 this is 1e-4..1.4e-4;
+# it only widens where fp32 itself cannot hold 1e-4: cfg5's outlier rows reach |lse| ~ 300,
+# where one fp32 ulp is 3e-5 and both the fp32 oracle and this kernel sit up to ~1e-6*|lse|
+# away from an fp64 evaluation (in different directions), so they can differ by ~2e-6*|lse|
+# -- see test_cfg5_lse_accuracy_against_fp64, which holds the kernel to the oracle's own
+# fp64 error.
+LSE_REL = 2e-6
 
 
 def _check(out, lse, ref_out, ref_lse, max_abs=MAX_ABS, mean_abs=MEAN_ABS, lse_abs=LSE_ABS):
+    ref_lse = ref_lse.float().to(lse.device)
     err = (out.float() - ref_out.float().to(out.device)).abs()
-    lerr = (lse.float() - ref_lse.float().to(lse.device)).abs()
+    lerr = (lse.float() - ref_lse).abs()
+    lse_tol = lse_abs + LSE_REL * ref_lse.abs()
     assert torch.isfinite(out.float()).all()
     assert err.max().item() <= max_abs, f"max abs {err.max().item():.3e}"
     assert err.mean().item() <= mean_abs, f"mean abs {err.mean().item():.3e}"
-    assert lerr.max().item() <= lse_abs, f"lse max abs {lerr.max().item():.3e}"
+    assert bool((lerr <= lse_tol).all()), f"lse max abs {lerr.max().item():.3e}"
 
 
 def _rand(shape, dtype, seed, device, scale=1.0):
@@ -151,6 +160,29 @@ def test_cfg5_outliers_sampled_slices(cuda_device):
     assert torch.isfinite(out.float()).all() and torch.isfinite(lse).all()
     # causal row 0 attends only key 0
     torch.testing.assert_close(out[:, :, 0].float(), v[:, :, 0].float(), atol=1e-3, rtol=0)
+
+
+def test_cfg5_lse_accuracy_against_fp64(cuda_device):
+    """On cfg5's outlier rows the kernel's LSE is as close to an fp64 evaluation as the fp32
+    oracle is (both sit at a few fp32 ulps of |lse|)."""
+    cfg = fa_inputs.CONFIGS["cfg5"]
+    q, k, v = fa_inputs.make_inputs(cfg, "cpu")
+    for b, h in [(0, 0), (1, 63)]:
+        qs, ks, vs = (t[b, h].cuda() for t in (q, k, v))
+        _, lse = ops.forward(qs[None, None], ks[None, None], vs[None, None], True, cfg.sm_scale)
+        S = qs.shape[0]
+        mask = torch.triu(torch.ones(S, S, dtype=torch.bool, device="cuda"), 1)
+        sc64 = ((qs.double() @ ks.double().T) * cfg.sm_scale).masked_fill_(mask, float("-inf"))
+        lse64 = torch.logsumexp(sc64, -1)
+        del sc64
+        sc32 = ((qs.float() @ ks.float().T) * cfg.sm_scale).masked_fill_(mask, float("-inf"))
+        lse32 = torch.logsumexp(sc32, -1)
+        del sc32
+        e_kernel = (lse[0, 0].double() - lse64).abs().max().item()
+        e_oracle = (lse32.double() - lse64).abs().max().item()
+        assert e_kernel <= max(1e-4, 1.5 * e_oracle), (e_kernel, e_oracle)
+        rel = ((lse[0, 0].double() - lse64).abs() / lse64.abs().clamp_min(1.0)).max().item()
+        assert rel <= 2e-6
 
 
 def test_gpu_fp32_reference_agrees_with_cpu_oracle(cuda_device):
