@@ -112,6 +112,12 @@ struct Geo {
                                     : TMEM_USED <= 256 ? 256
                                                        : 512;
   static constexpr int NUM_THREADS = 128 + 128 * QT;
+  // Register split for QT == 2: 128 x 80 + 256 x 208 = 63488 <= 384 threads x 168 = 64512.
+  static constexpr int REG_LAUNCH = 168;
+  static constexpr int REG_LOW = 80;
+  static constexpr int REG_HIGH = 208;
+  static_assert(QT != 2 || 128 * REG_LOW + 256 * REG_HIGH <= NUM_THREADS * REG_LAUNCH,
+                "register split must fit the launch allocation");
   static constexpr uint32_t LAYOUT = SWZ == 128 ? 2u : (SWZ == 64 ? 4u : 6u);
   // V is the MN-major operand of P.V.  For tf32 that operand needs the 32-byte-atom 128B
   // swizzle (descriptor code 1, 4-row K groups; TMA CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B).
@@ -170,16 +176,119 @@ __device__ __forceinline__ bool wait_bar(Shared* sh, uint32_t bar, uint32_t pari
   }
 }
 
+// Round two floats to a packed 16-bit pair: `lo` in bits 0-15, `hi` in bits 16-31
+// (cvt.rn.{bf16,f16}x2.f32 d, a, b puts a in the upper half).
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, __nv_bfloat16*) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
 }
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, __half*) {
-  __half2 v = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
 }
 
 // --------------------------------------------------------------------------------------
+// exp2 on the FMA pipe, for a pair of lanes.  2^x = 2^n * 2^f with n = round(x) taken from the
+// low mantissa bits of x + 1.5*2^23 and f = x - n in [-0.5, 0.5]; 2^f is a degree-4 polynomial
+// minimising the relative error on that interval (coefficients from csrc/exp2_poly_fit.py, max
+// relative error 2.7e-6 in fp32 Horner form).  2^n is applied by adding n to the exponent
+// field.  x is clamped at -127 so the exponent never underflows past zero (2^-127 ~ 0 here).
+#ifndef FA_POLY_PAIRS_OF_8
+#define FA_POLY_PAIRS_OF_8 0  // element pairs out of every 8 that use the polynomial
+#endif
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c0 = 9.999992847e-01f, c1 = 6.931217909e-01f, c2 = 2.402474433e-01f,
+                  c3 = 5.591785908e-02f, c4 = 9.570101276e-03f;
+  x.x = fmaxf(x.x, -127.f);
+  x.y = fmaxf(x.y, -127.f);
+  const float2 t = fadd2(x, make_float2(kRound, kRound));
+  const float2 n = fadd2(t, make_float2(-kRound, -kRound));
+  const float2 f = ffma2(n, make_float2(-1.f, -1.f), x);
+  float2 q = ffma2(make_float2(c4, c4), f, make_float2(c3, c3));
+  q = ffma2(q, f, make_float2(c2, c2));
+  q = ffma2(q, f, make_float2(c1, c1));
+  q = ffma2(q, f, make_float2(c0, c0));
+  // bits(t) = bits(kRound) + n and bits(kRound) << 23 == 0 (mod 2^32): (bits(t) << 23) == n << 23
+  q.x = __int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23));
+  q.y = __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23));
+  return q;
+}
+
+// Row maximum of BN logits with 3-input max, 8 independent chains.
+template <int BN>
+__device__ __forceinline__ float row_max(const float* s) {
+  float e[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) e[t] = fmaxf(s[2 * t], s[2 * t + 1]);
+#pragma unroll
+  for (int k = 16; k < BN; k += 16) {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) e[t] = fmax3(e[t], s[k + 2 * t], s[k + 2 * t + 1]);
+  }
+  return fmax3(fmax3(e[0], e[1], e[2]), fmax3(e[3], e[4], e[5]), fmaxf(e[6], e[7]));
+}
+
+// P = 2^(s*sl2 + neg_m) for an unmasked row, written to TMEM at tP in two halves: the store of
+// the first half is in flight while the second half is computed (the caller waits once; the
+// store reads its source registers asynchronously, so finer chunking would pin more of them).
+// Returns the row sum of the unrounded fp32 values; with WITH_MAX it also returns max(s) through
+// *mx, computed in the same pass (ALU work that overlaps the MUFU exponentials).  s is left
+// intact.  A fixed share of the element pairs can go through the FMA-pipe polynomial.
+template <typename T, int BN, bool WITH_MAX>
+__device__ __forceinline__ float exp2_row_store(const float* s, float sl2, float neg_m, uint32_t tP,
+                                                float* mx) {
+  constexpr int HALF = BN / 2;
+  constexpr int PW = Elt<T>::kTf32 ? HALF : HALF / 2;  // 32-bit TMEM words per half row
+  const float2 sc = make_float2(sl2, sl2);
+  const float2 nm = make_float2(neg_m, neg_m);
+  float2 acc[4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) acc[t] = make_float2(0.f, 0.f);
+  float e[8];
+  if constexpr (WITH_MAX) {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) e[t] = -INFINITY;
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t pk[PW];
+#pragma unroll
+    for (int k = h * HALF; k < (h + 1) * HALF; k += 2) {
+      const float2 x = ffma2(make_float2(s[k], s[k + 1]), sc, nm);
+      float2 pr;
+      if (((k >> 1) & 7) < FA_POLY_PAIRS_OF_8) {
+        pr = exp2_poly2(x);
+      } else {
+        pr.x = ex2_approx(x.x);
+        pr.y = ex2_approx(x.y);
+      }
+      acc[(k >> 1) & 3] = fadd2(acc[(k >> 1) & 3], pr);
+      if constexpr (WITH_MAX) e[(k >> 1) & 7] = fmax3(e[(k >> 1) & 7], s[k], s[k + 1]);
+      const int w = (k - h * HALF) >> 1;
+      if constexpr (Elt<T>::kTf32) {
+        pk[2 * w] = __float_as_uint(pr.x);
+        pk[2 * w + 1] = __float_as_uint(pr.y);
+      } else {
+        pk[w] = pack2(pr.x, pr.y, static_cast<T*>(nullptr));
+      }
+    }
+#pragma unroll
+    for (int w = 0; w < PW; w += 32) {
+      if constexpr (PW >= 32)
+        tmem_st32(tP + h * PW + w, pk + w);
+      else
+        tmem_st16(tP + h * PW + w, pk + w);
+    }
+  }
+  if constexpr (WITH_MAX)
+    *mx = fmax3(fmax3(e[0], e[1], e[2]), fmax3(e[3], e[4], e[5]), fmaxf(e[6], e[7]));
+  const float2 a = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
+  return a.x + a.y;
+}
+
 template <typename T, int D, int BN, int QT>
 __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
     fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -259,6 +368,12 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
 
+  // QT == 2: the producer/MMA warpgroup (warps 0-3) hands registers to the two softmax
+  // warpgroups.  The split sums to the launch allocation (the host refuses to launch a build
+  // whose per-thread count is not REG_LAUNCH).  Each setmaxnreg sits at the top of its role's
+  // branch so the register limit it sets covers that role's code.
+  if (warp < 4) {
+    if constexpr (QT == 2) setmaxnreg_dec<G::REG_LOW>();
   if (warp == 0) {
     // ================================================================ TMA producer
     if (lane == 0) {
@@ -325,68 +440,80 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
     if (lane == 0 && n_max > 0) {
       bool ok = wait_bar(sh, smem_u32(&sh->q_full), 0, p.status);
       tc_fence_after();
-      // ring position of K_j is 2j, of V_j is 2j+1
-      auto slot_of = [&](int pos) { return pos % stages; };
-      auto par_of = [&](int pos) { return static_cast<uint32_t>((pos / stages) & 1); };
-      const uint32_t q_base = smem_u32(q_smem);
-      const uint32_t kv_base = smem_u32(kv_smem);
+      // This single thread shares its SM sub-partition with two busy softmax warps, so its
+      // instruction stream is kept minimal: descriptors are built once and their start-address
+      // field (bits 0-13 = address >> 4) is advanced by adding byte offsets >> 4 (shared memory
+      // stays below 256 KiB, so the field never carries into the next one); ring slots and
+      // phases advance incrementally.
+      const uint64_t q_desc = make_smem_desc(smem_u32(q_smem), 16, 8 * G::SWZ, G::LAYOUT);
+      const uint64_t k_desc = make_smem_desc(smem_u32(kv_smem), 16, 8 * G::SWZ, G::LAYOUT);
+      const uint64_t v_desc =
+          make_smem_desc(smem_u32(kv_smem), G::KV_BLK_BYTES, G::V_SBO, G::V_LAYOUT);
+      constexpr uint32_t kSlotStep = G::KV_TILE_BYTES >> 4;
+      const uint32_t full0 = smem_u32(&sh->full[0]);
+      const uint32_t empty0 = smem_u32(&sh->empty[0]);
 
       // S_i = Q_i K^T : A = Q tile (K-major), B = K tile (K-major), both SWZ-swizzled.
       auto issue_s = [&](int i, int kslot) {
-        const uint32_t a0 = q_base + i * G::Q_TILE_BYTES;
-        const uint32_t b0 = kv_base + kslot * G::KV_TILE_BYTES;
+        const uint64_t a0 = q_desc + static_cast<uint64_t>((i * G::Q_TILE_BYTES) >> 4);
+        const uint64_t b0 = k_desc + static_cast<uint64_t>(kslot * kSlotStep);
         const uint32_t d = tmem + G::TMEM_S + i * BN;
 #pragma unroll
         for (int c = 0; c < G::NBLK; ++c) {
 #pragma unroll
           for (int kk = 0; kk < G::KSTEPS_PER_BLK; ++kk) {
-            const uint64_t ad = make_smem_desc(a0 + c * G::Q_BLK_BYTES + kk * 32, 16, 8 * G::SWZ,
-                                               G::LAYOUT);
-            const uint64_t bd = make_smem_desc(b0 + c * G::KV_BLK_BYTES + kk * 32, 16, 8 * G::SWZ,
-                                               G::LAYOUT);
-            const uint32_t acc = (c | kk) ? 1u : 0u;
+            const uint64_t ad = a0 + static_cast<uint64_t>((c * G::Q_BLK_BYTES + kk * 32) >> 4);
+            const uint64_t bd = b0 + static_cast<uint64_t>((c * G::KV_BLK_BYTES + kk * 32) >> 4);
             if constexpr (Elt<T>::kTf32)
-              mma_tf32_ss(d, ad, bd, G::IDESC_S, acc);
+              mma_tf32_ss(d, ad, bd, G::IDESC_S, (c | kk) ? 1u : 0u);
             else
-              mma_f16_ss(d, ad, bd, G::IDESC_S, acc);
+              mma_f16_ss(d, ad, bd, G::IDESC_S, (c | kk) ? 1u : 0u);
           }
         }
       };
       // O_i (+)= P_i V : A = P_i in TMEM, B = V tile (MN-major: rows = keys, cols = head dim).
-      auto issue_pv = [&](int i, int vslot, bool accumulate) {
-        const uint32_t b0 = kv_base + vslot * G::KV_TILE_BYTES;
+      auto issue_pv = [&](int i, int vslot, uint32_t acc0) {
+        const uint64_t b0 = v_desc + static_cast<uint64_t>(vslot * kSlotStep);
         const uint32_t d = tmem + G::TMEM_O + i * D;
         const uint32_t a = tmem + G::TMEM_S + i * BN;
 #pragma unroll
         for (int kk = 0; kk < BN / G::MMA_K; ++kk) {
-          // MMA_K keys = MMA_K rows of V = MMA_K/8 eight-row groups of SWZ bytes each
-          const uint64_t bd = make_smem_desc(b0 + kk * G::MMA_K * G::SWZ, G::KV_BLK_BYTES,
-                                             G::V_SBO, G::V_LAYOUT);
-          const uint32_t acc = (accumulate || kk > 0) ? 1u : 0u;
-          // each TMEM column holds 4 bytes of P: MMA_K elements = MMA_K*EB/4 columns
+          // MMA_K keys = MMA_K rows of V; each TMEM column of P holds 4 bytes
+          const uint64_t bd = b0 + static_cast<uint64_t>((kk * G::MMA_K * G::SWZ) >> 4);
           const uint32_t acol = static_cast<uint32_t>(kk * G::MMA_K * G::EB / 4);
           if constexpr (Elt<T>::kTf32)
-            mma_tf32_ts(d, a + acol, bd, G::IDESC_O, acc);
+            mma_tf32_ts(d, a + acol, bd, G::IDESC_O, kk > 0 ? 1u : acc0);
           else
-            mma_f16_ts(d, a + acol, bd, G::IDESC_O, acc);
+            mma_f16_ts(d, a + acol, bd, G::IDESC_O, kk > 0 ? 1u : acc0);
+        }
+      };
+      auto advance = [&](int& sl, uint32_t& ph) {
+        if (++sl == stages) {
+          sl = 0;
+          ph ^= 1u;
         }
       };
 
-      if (ok) ok = wait_bar(sh, smem_u32(&sh->full[slot_of(0)]), par_of(0), p.status);
+      // ring: K_0, V_0, K_1, V_1, ...  (K_j at position 2j, V_j at 2j+1)
+      if (ok) ok = wait_bar(sh, full0, 0, p.status);
       if (ok) {
         tc_fence_after();
 #pragma unroll
         for (int i = 0; i < QT; ++i) {
           if (n_kv[i] == 0) continue;
-          issue_s(i, slot_of(0));
+          issue_s(i, 0);
           mma_commit(smem_u32(&sh->s_full[i]));
         }
-        mma_commit(smem_u32(&sh->empty[slot_of(0)]));
+        mma_commit(empty0);
       }
+      int vs = 0;
+      uint32_t vph = 0;
+      advance(vs, vph);  // V_0
       for (int j = 0; j < n_max && ok; ++j) {
-        const int vpos = 2 * j + 1;
-        const int kpos = 2 * j + 2;
-        ok = wait_bar(sh, smem_u32(&sh->full[slot_of(vpos)]), par_of(vpos), p.status);
+        int ks = vs;
+        uint32_t kph = vph;
+        advance(ks, kph);  // K_{j+1}
+        ok = wait_bar(sh, full0 + 8u * vs, vph, p.status);
         if (!ok) break;
         bool k_ready = false;
 #pragma unroll
@@ -395,22 +522,25 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
           ok = wait_bar(sh, smem_u32(&sh->p_full[i]), static_cast<uint32_t>(j & 1), p.status);
           if (!ok) break;
           tc_fence_after();
-          issue_pv(i, slot_of(vpos), j > 0);
+          issue_pv(i, vs, j > 0 ? 1u : 0u);
           if (j == n_kv[i] - 1) mma_commit(smem_u32(&sh->o_full[i]));
           if (j + 1 < n_kv[i]) {
             if (!k_ready) {
-              ok = wait_bar(sh, smem_u32(&sh->full[slot_of(kpos)]), par_of(kpos), p.status);
+              ok = wait_bar(sh, full0 + 8u * ks, kph, p.status);
               if (!ok) break;
               tc_fence_after();
               k_ready = true;
             }
-            issue_s(i, slot_of(kpos));
+            issue_s(i, ks);
             mma_commit(smem_u32(&sh->s_full[i]));
           }
         }
         if (!ok) break;
-        mma_commit(smem_u32(&sh->empty[slot_of(vpos)]));
-        if (k_ready) mma_commit(smem_u32(&sh->empty[slot_of(kpos)]));
+        mma_commit(empty0 + 8u * vs);
+        if (k_ready) mma_commit(empty0 + 8u * ks);
+        vs = ks;
+        vph = kph;
+        advance(vs, vph);  // V_{j+1}
       }
       // All MMAs issued by this thread must finish before TMEM is released.
       mma_commit(smem_u32(&sh->mma_done));
@@ -421,7 +551,9 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
         }
       }
     }
-  } else if (warp >= 4) {
+  }
+  } else {
+    if constexpr (QT == 2) setmaxnreg_inc<G::REG_HIGH>();
     // ================================================================ softmax warpgroups
     const int i = (warp - 4) >> 2;  // query tile
     const int wq = warp & 3;        // TMEM lane quarter
@@ -457,47 +589,24 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
         lim = max(0, min(lim, BN));
       }
       const bool masked = tail || diag;
+      const bool fast = use_max && !masked;
       const float fill = use_max ? -INFINITY : INFINITY;
 
-      // row extreme (max for scale >= 0, min for scale < 0), 8 independent chains
-      float e8[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) e8[t] = fill;
-      if (masked) {
-#pragma unroll
-        for (int k = 0; k < BN; ++k) {
-          const float v = (k < lim) ? s[k] : fill;
-          e8[k & 7] = use_max ? fmaxf(e8[k & 7], v) : fminf(e8[k & 7], v);
-        }
-      } else if (use_max) {
-#pragma unroll
-        for (int k = 0; k < BN; ++k) e8[k & 7] = fmaxf(e8[k & 7], s[k]);
-      } else {
-#pragma unroll
-        for (int k = 0; k < BN; ++k) e8[k & 7] = fminf(e8[k & 7], s[k]);
-      }
-      float ext = e8[0];
-#pragma unroll
-      for (int t = 1; t < 8; ++t) ext = use_max ? fmaxf(ext, e8[t]) : fminf(ext, e8[t]);
-
-      const float m_tile = ext * sl2;                // NaN only when a row is fully masked and scale == 0
-      const float m_new = fmaxf(m_used, m_tile);     // fmaxf drops a NaN operand
-      const bool need = m_new > m_used + RESCALE_LOG2;
-      float alpha = 1.f;
-      if (need) {
-        alpha = ex2_approx(m_used - m_new);  // m_used = -inf gives 0
-        l *= alpha;
-        m_used = m_new;
-      }
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // O_i holds sum over steps < j (S_i(j) completion implies P_i(j-1) V_{j-1} done).
+      // O_i holds the sum over steps < j (S_i(j) completion implies P_i(j-1) V_{j-1} is done),
+      // so it can be rescaled here, before P_i(j) is released.  Warp-collective.
+      auto rescale_o = [&](float alpha) {
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t o[32];
           tmem_ld32(tO + c * 32, o);
           tmem_wait_ld();
+          const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
-          for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
+          for (int t = 0; t < 32; t += 2) {
+            const float2 v = fmul2(make_float2(__uint_as_float(o[t]), __uint_as_float(o[t + 1])), a2);
+            o[t] = __float_as_uint(v.x);
+            o[t + 1] = __float_as_uint(v.y);
+          }
           tmem_st32(tO + c * 32, o);
         }
         if constexpr (D % 32 == 16) {
@@ -508,40 +617,90 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
           for (int t = 0; t < 16; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
           tmem_st16(tO + (D / 32) * 32, o);
         }
-      }
+      };
 
-      // p = 2^(s*scale_log2 - m_used); masked columns -> 0
-      const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
-      float l8[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) l8[t] = 0.f;
-      if (masked) {
-#pragma unroll
-        for (int k = 0; k < BN; ++k) {
-          const float x = (k < lim) ? fmaf(s[k], sl2, neg_m) : -INFINITY;
-          s[k] = ex2_approx(x);
-          l8[k & 7] += s[k];
+      if (fast && j > 0) {
+        // Optimistic pass: exponentiate against the current base and take the row max in the
+        // same pass.  Exact unless some row's max moved past base + RESCALE_LOG2; then (rare)
+        // that row takes the new base, O is rescaled, and the warp recomputes P.
+        float mx;
+        const float base = (m_used == -INFINITY) ? 0.f : -m_used;
+        float lt = exp2_row_store<T, BN, true>(s, sl2, base, tS, &mx);
+        const float m_tile = mx * sl2;
+        const bool need = m_tile > m_used + RESCALE_LOG2;
+        if (__any_sync(0xffffffffu, need)) {
+          float alpha = 1.f;
+          if (need) {
+            alpha = ex2_approx(m_used - m_tile);  // m_used = -inf gives 0
+            l *= alpha;
+            m_used = m_tile;
+          }
+          rescale_o(alpha);
+          tmem_wait_st();  // the first pass's P stores land before they are overwritten
+          lt = exp2_row_store<T, BN, false>(s, sl2, -m_used, tS, nullptr);
         }
+        l += lt;
       } else {
+        // row extreme (max for scale >= 0, min for scale < 0), 8 independent chains
+        float e8[8];
 #pragma unroll
-        for (int k = 0; k < BN; ++k) {
-          s[k] = ex2_approx(fmaf(s[k], sl2, neg_m));
-          l8[k & 7] += s[k];
+        for (int t = 0; t < 8; ++t) e8[t] = fill;
+        if (fast) {
+          e8[0] = row_max<BN>(s);
+        } else if (masked) {
+#pragma unroll
+          for (int k = 0; k < BN; ++k) {
+            const float v = (k < lim) ? s[k] : fill;
+            e8[k & 7] = use_max ? fmaxf(e8[k & 7], v) : fminf(e8[k & 7], v);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < BN; ++k) e8[k & 7] = fminf(e8[k & 7], s[k]);
         }
-      }
-      l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+        float ext = e8[0];
+#pragma unroll
+        for (int t = 1; t < 8; ++t) ext = use_max ? fmaxf(ext, e8[t]) : fminf(ext, e8[t]);
 
-      // P back into TMEM (over the first P_COLS columns of S_i)
-      if constexpr (Elt<T>::kTf32) {
+        const float m_tile = ext * sl2;             // NaN only when a row is fully masked and scale == 0
+        const float m_new = fmaxf(m_used, m_tile);  // fmaxf drops a NaN operand
+        const bool need = m_new > m_used + RESCALE_LOG2;
+        float alpha = 1.f;
+        if (need) {
+          alpha = ex2_approx(m_used - m_new);  // m_used = -inf gives 0
+          l *= alpha;
+          m_used = m_new;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, need)) rescale_o(alpha);
+
+        // p = 2^(s*scale_log2 - m_used); masked columns -> 0
+        const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+        if (fast) {
+          l += exp2_row_store<T, BN, false>(s, sl2, neg_m, tS, nullptr);  // also writes P
+        } else {
+          float l8[8];
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-          tmem_st32(tS + c * 32, reinterpret_cast<const uint32_t*>(s) + c * 32);
-      } else {
-        uint32_t pk[BN / 2];
+          for (int t = 0; t < 8; ++t) l8[t] = 0.f;
 #pragma unroll
-        for (int k = 0; k < BN / 2; ++k) pk[k] = pack2(s[2 * k], s[2 * k + 1], static_cast<T*>(nullptr));
+          for (int k = 0; k < BN; ++k) {
+            const float x = (k < lim) ? fmaf(s[k], sl2, neg_m) : -INFINITY;
+            s[k] = ex2_approx(x);
+            l8[k & 7] += s[k];
+          }
+          l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+          // P back into TMEM (over the first P_COLS columns of S_i)
+          if constexpr (Elt<T>::kTf32) {
 #pragma unroll
-        for (int c = 0; c < BN / 64; ++c) tmem_st32(tS + c * 32, pk + c * 32);
+            for (int c = 0; c < BN / 32; ++c)
+              tmem_st32(tS + c * 32, reinterpret_cast<const uint32_t*>(s) + c * 32);
+          } else {
+            uint32_t pk[BN / 2];
+#pragma unroll
+            for (int k = 0; k < BN / 2; ++k)
+              pk[k] = pack2(s[2 * k], s[2 * k + 1], static_cast<T*>(nullptr));
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c) tmem_st32(tS + c * 32, pk + c * 32);
+          }
+        }
       }
       tmem_wait_st();
       tc_fence_before();

@@ -50,6 +50,20 @@ int launch_kernel(const LaunchPlan& lp) {
   using G = Geo<T, D, BN, QT>;
   auto kern = fa_fwd_sm100_kernel<T, D, BN, QT>;
   const int smem = G::smem_bytes(lp.params.stages);
+  if constexpr (QT == 2) {
+    // setmaxnreg redistributes exactly the launch allocation; refuse to launch a build whose
+    // per-thread register count differs (the split would not add up).
+    static int regs_ok = 0;  // 0 unknown, 1 ok, -1 mismatch
+    if (regs_ok == 0) {
+      cudaFuncAttributes fattr{};
+      regs_ok = (cudaFuncGetAttributes(&fattr, kern) == cudaSuccess &&
+                 fattr.numRegs == G::REG_LAUNCH)
+                    ? 1
+                    : -1;
+      (void)cudaGetLastError();
+    }
+    if (regs_ok != 1) return -7;
+  }
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
       cudaSuccess) {
     (void)cudaGetLastError();

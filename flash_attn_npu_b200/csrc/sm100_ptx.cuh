@@ -200,6 +200,9 @@ __device__ __forceinline__ void tmem_wait_st() {
 }
 
 // 32 lanes x 32 consecutive 32-bit columns: thread t of the warp receives lane (base+t).
+// TMEM loads/stores carry no "memory" clobber (they touch no generic memory, and a clobber
+// would pin register arrays in local memory); their order against tcgen05.wait / fences /
+// mbarrier ops is kept because every one of those is asm volatile.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -233,8 +236,7 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
       "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
       "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
-      "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
+      "r"(r[29]), "r"(r[30]), "r"(r[31]));
 }
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
@@ -243,8 +245,7 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
       "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
-      "r"(r[15])
-      : "memory");
+      "r"(r[15]));
 }
 
 // ------------------------------------------------------------ descriptors
@@ -270,6 +271,50 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_format, bool b_mn_
                                                   int n) {
   return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((b_mn_major ? 1u : 0u) << 16) |
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// Warpgroup register reallocation (all four warps of the warpgroup execute it).
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): one instruction for two lanes of math.
+union F2U {
+  float2 f;
+  uint64_t u;
+};
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  F2U A, B, C, D;
+  A.f = a;
+  B.f = b;
+  C.f = c;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(D.u) : "l"(A.u), "l"(B.u), "l"(C.u));
+  return D.f;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  F2U A, B, D;
+  A.f = a;
+  B.f = b;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(D.u) : "l"(A.u), "l"(B.u));
+  return D.f;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  F2U A, B, D;
+  A.f = a;
+  B.f = b;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(D.u) : "l"(A.u), "l"(B.u));
+  return D.f;
+}
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
