@@ -18,6 +18,8 @@ FA_DTYPE_FP16 = 0
 FA_DTYPE_BF16 = 1
 FA_DTYPE_FP32 = 2
 
+FA_FLAG_FP32_TF32 = 1
+
 FA_OK = 0
 FA_ERR_INVALID_ARG = -1
 FA_ERR_UNSUPPORTED_HEAD_DIM = -2
@@ -71,6 +73,7 @@ class FaFwdArgs(ctypes.Structure):
         ("sm_scale", ctypes.c_float),
         ("tile", FaTileConfig),
         ("dev_status", ctypes.c_void_p),
+        ("flags", ctypes.c_int32),
     ]
 
 
@@ -152,7 +155,7 @@ def max_stages(head_dim: int, dtype_code: int, block_m: int, block_n: int) -> in
 def make_args(*, q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, batch, heads, seqlen, head_dim,
               q_stride, k_stride, v_stride, o_stride, dtype_code, causal, sm_scale,
               block_m=0, block_n=0, num_stages=0, persistent_ctas=0,
-              status_ptr=None) -> FaFwdArgs:
+              status_ptr=None, flags=0) -> FaFwdArgs:
     a = FaFwdArgs()
     a.struct_size = ctypes.sizeof(FaFwdArgs)
     a.q, a.k, a.v, a.o, a.lse = q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr
@@ -167,6 +170,7 @@ def make_args(*, q_ptr, k_ptr, v_ptr, o_ptr, lse_ptr, batch, heads, seqlen, head
     a.sm_scale = float(sm_scale)
     a.tile = FaTileConfig(int(block_m), int(block_n), int(num_stages), int(persistent_ctas))
     a.dev_status = status_ptr
+    a.flags = int(flags)
     return a
 
 

@@ -27,6 +27,7 @@ LIB_PATH = PKG_DIR / LIB_NAME
 
 SOURCES = [
     "fa_fwd_api.cu",
+    "fa_fwd_fp32.cu",
     "fa_fwd_d16.cu",
     "fa_fwd_d32.cu",
     "fa_fwd_d64.cu",

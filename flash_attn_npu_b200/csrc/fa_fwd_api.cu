@@ -19,6 +19,7 @@
 #include <mutex>
 
 #include "../../include/fa_fwd_sm100.h"
+#include "fa_fp32.h"
 #include "fa_launch.h"
 
 namespace {
@@ -123,7 +124,13 @@ int validate(const FaFwdArgs* a) {
   if (!a->q || !a->k || !a->v || !a->o || !a->lse) return FA_ERR_INVALID_ARG;
   if (!std::isfinite(a->sm_scale)) return FA_ERR_INVALID_ARG;
   if (reinterpret_cast<uintptr_t>(a->lse) % 4 != 0) return FA_ERR_MISALIGNED;
+  if (a->flags & ~FA_FLAG_FP32_TF32) return FA_ERR_INVALID_ARG;
   return FA_OK;
+}
+
+// fp32 inputs without FA_FLAG_FP32_TF32 take the CUDA-core kernel.
+bool use_fp32_simt(const FaFwdArgs* a) {
+  return a->dtype == FA_DTYPE_FP32 && !(a->flags & FA_FLAG_FP32_TF32);
 }
 
 int resolve_tile(const FaFwdArgs* a, FaTileConfig* t) {
@@ -202,6 +209,7 @@ int fa_fwd_sm100_max_stages(int64_t head_dim, int32_t dtype, int32_t block_m, in
 
 int64_t fa_fwd_sm100_grid_size(const FaFwdArgs* a) {
   if (validate(a) != FA_OK) return -1;
+  if (use_fp32_simt(a)) return ((a->seqlen + 63) / 64) * a->batch * a->heads;
   FaTileConfig t;
   if (resolve_tile(a, &t) != FA_OK) return -1;
   const int64_t nq = (a->seqlen + t.block_m - 1) / t.block_m;
@@ -217,6 +225,24 @@ int fa_fwd_sm100(const FaFwdArgs* a, void* stream) {
     return FA_ERR_DEVICE;
   }
   if (!device_ok(dev)) return FA_ERR_DEVICE;
+  if (use_fp32_simt(a)) {
+    fa::Fp32Params fp{};
+    fp.batch = a->batch;
+    fp.heads = a->heads;
+    fp.seqlen = static_cast<int>(a->seqlen);
+    fp.head_dim = static_cast<int>(a->head_dim);
+    for (int i = 0; i < 3; ++i) {
+      fp.q_stride[i] = a->q_stride[i];
+      fp.k_stride[i] = a->k_stride[i];
+      fp.v_stride[i] = a->v_stride[i];
+      fp.o_stride[i] = a->o_stride[i];
+    }
+    fp.causal = a->causal ? 1 : 0;
+    fp.scale_log2 = a->sm_scale * fa::kLog2e;
+    return fa::launch_fp32_simt(static_cast<const float*>(a->q), static_cast<const float*>(a->k),
+                                static_cast<const float*>(a->v), static_cast<float*>(a->o),
+                                a->lse, fp, static_cast<cudaStream_t>(stream));
+  }
   FaTileConfig t;
   rc = resolve_tile(a, &t);
   if (rc != FA_OK) return rc;

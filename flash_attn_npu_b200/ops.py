@@ -66,13 +66,14 @@ def _tma_view(t: torch.Tensor) -> torch.Tensor:
 def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_scale: float, *,
             block_m: int = 0, block_n: int = 0, num_stages: int = 0, persistent_ctas: int = 0,
             out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
-            status: torch.Tensor | None = None):
+            status: torch.Tensor | None = None, fp32_tf32: bool = False):
     """Run attention forward on the B200 kernel; returns (out, lse).
 
     `block_m/block_n/num_stages/persistent_ctas` = 0 picks the library default.  `out` and
     `lse` may be preallocated (same shape/dtype rules as the freshly allocated ones).
     `status`, if given, is a device int32 tensor of one element that must be zero; a pipeline
-    timeout inside the kernel writes a negative code there.
+    timeout inside the kernel writes a negative code there.  float32 inputs run in fp32 on the
+    CUDA cores unless `fp32_tf32` selects the (faster, TF32-rounded) tensor-core kernel.
     """
     validate_inputs(q, k, v)
     z, h, n_ctx, head_dim = q.shape
@@ -104,7 +105,8 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_
         o_stride=out.stride()[:3], dtype_code=code, causal=causal, sm_scale=sm_scale,
         block_m=block_m, block_n=block_n, num_stages=num_stages,
         persistent_ctas=persistent_ctas,
-        status_ptr=(status.data_ptr() if status is not None else None))
+        status_ptr=(status.data_ptr() if status is not None else None),
+        flags=_native.FA_FLAG_FP32_TF32 if fp32_tf32 else 0)
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
         try:

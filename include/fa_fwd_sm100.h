@@ -36,9 +36,13 @@
 extern "C" {
 #endif
 
-/* Element types (the reference accepts fp16 and bf16, flash_attention_forward.py:1306-1312;
- * fp32 inputs run through the tf32 tensor-core path). */
+/* Element types (the reference accepts fp16 and bf16, flash_attention_forward.py:1306-1312).
+ * fp32 inputs run on the CUDA cores in fp32 by default, or on the tensor cores in TF32 with
+ * FA_FLAG_FP32_TF32 (faster; TF32 rounding moves the logsumexp by ~1e-3). */
 enum FaDtype { FA_DTYPE_FP16 = 0, FA_DTYPE_BF16 = 1, FA_DTYPE_FP32 = 2 };
+
+/* FaFwdArgs.flags bits. */
+enum FaFlags { FA_FLAG_FP32_TF32 = 1 };
 
 /* Return codes. */
 enum FaStatus {
@@ -79,8 +83,9 @@ typedef struct FaFwdArgs {
   int32_t dtype;  /* enum FaDtype */
   int32_t causal; /* 0 / 1: query i attends keys <= i (reference STAGE=3) */
   float sm_scale; /* softmax scale applied to q.k */
-  FaTileConfig tile;
+  FaTileConfig tile;   /* tensor-core kernels only */
   int32_t* dev_status; /* optional device int, 0 on success */
+  int32_t flags;       /* FaFlags */
 } FaFwdArgs;
 
 /* Launch the forward pass.  Returns FA_OK or a negative FaStatus.

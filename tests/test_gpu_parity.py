@@ -94,6 +94,32 @@ def test_matrix_head_dim_dtype_tile(head_dim, dtype, causal, tile, cuda_device):
     _run_and_check(2, 3, 333, head_dim, dtype, causal, bm, bn, seed=head_dim)
 
 
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("head_dim", [16, 32, 64, 128, 256])
+@pytest.mark.parametrize("seqlen", [1, 77, 128, 300])
+def test_fp32_inputs_cuda_core_path(head_dim, causal, seqlen, cuda_device):
+    """float32 inputs: fp32 arithmetic throughout, held to the full bar (LSE included)."""
+    _run_and_check(2, 2, seqlen, head_dim, torch.float32, causal, seed=head_dim + seqlen)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("head_dim", [32, 64, 128])
+@pytest.mark.parametrize("tile", [(128, 64), (128, 128), (256, 64)], ids=lambda t: f"bm{t[0]}bn{t[1]}")
+def test_fp32_inputs_tf32_tensor_core_mode(head_dim, causal, tile, cuda_device):
+    """Opt-in TF32 tensor-core mode: output within the parity bar; TF32 rounding of Q.K^T moves
+    the logsumexp by ~1e-3, so LSE is held to 5e-3 here (the default fp32 path meets 1e-4)."""
+    if tile == (256, 64) and head_dim > 64:
+        pytest.skip("no two-tile TF32 kernel at head_dim 128")
+    q = _rand((1, 2, 300, head_dim), torch.float32, 1, "cuda")
+    k = _rand((1, 2, 300, head_dim), torch.float32, 2, "cuda")
+    v = _rand((1, 2, 300, head_dim), torch.float32, 3, "cuda")
+    out, lse = ops.forward(q, k, v, causal, head_dim ** -0.5, block_m=tile[0], block_n=tile[1],
+                           fp32_tf32=True)
+    ro, rl = attention_ref_torch(q.cpu(), k.cpu(), v.cpu(), causal, head_dim ** -0.5)
+    torch.cuda.synchronize()
+    _check(out, lse, ro, rl, lse_abs=5e-3)
+
+
 @pytest.mark.parametrize("seqlen", [1, 2, 63, 64, 65, 127, 128, 129, 255, 256, 257, 1000, 2049])
 @pytest.mark.parametrize("causal", [False, True])
 def test_ragged_sequence_lengths(seqlen, causal, cuda_device):
@@ -134,6 +160,10 @@ def _config_check(name, slices=None, device="cuda"):
 
 def test_cfg1_fp16(cuda_device):
     _config_check("cfg1_fp16")
+
+
+def test_cfg1_fp32(cuda_device):
+    _config_check("cfg1_fp32")
 
 
 def test_cfg2_full(cuda_device):
