@@ -137,6 +137,16 @@ def _launch_kernel(q, k, v, causal, sm_scale, bm=None, bn=None):
                         persistent_ctas=cfg.persistent_ctas)
 
 
+def _launch_kernel_config(q, k, v, causal, sm_scale, config):
+    """Launch with a full sm_100a tile config (dict with BLOCK_M, BLOCK_N and optionally
+    NUM_STAGES, PERSISTENT_CTAS -- the tuner's candidates); -> (out, lse)."""
+    _validate_inputs(q, k, v)
+    cfg = _tiling.TileConfig.from_preset(config)
+    return _ops.forward(q, k, v, bool(causal), float(sm_scale), block_m=cfg.block_m,
+                        block_n=cfg.block_n, num_stages=cfg.num_stages,
+                        persistent_ctas=cfg.persistent_ctas)
+
+
 def attention(q, k, v, causal, sm_scale, BM=None, BN=None, return_lse=False):
     out, lse = _launch_kernel(q, k, v, causal, sm_scale, bm=BM, bn=BN)
     if return_lse:
