@@ -138,7 +138,10 @@ def _launch_kernel(q, k, v, causal, sm_scale, bm=None, bn=None):
     """Validate, allocate `out` (empty_like q) and fp32 `lse` [Z,H,N], launch; -> (out, lse)."""
     _validate_inputs(q, k, v)
     z, h, n_ctx, head_dim = q.shape
-    cfg, _ = _resolve_config(z, h, n_ctx, head_dim, causal, q.dtype, bm, bn)
+    cfg, source = _resolve_config(z, h, n_ctx, head_dim, causal, q.dtype, bm, bn)
+    if _ops.is_v_fp8(q, v) and source != "override":
+        # presets are tuned for 16-bit V; the fp8-V kernel takes the library default tile
+        cfg = _tiling.TileConfig(0, 0, 0, cfg.persistent_ctas)
     return _ops.forward(q, k, v, bool(causal), float(sm_scale), block_m=cfg.block_m,
                         block_n=cfg.block_n, num_stages=cfg.num_stages,
                         persistent_ctas=cfg.persistent_ctas)

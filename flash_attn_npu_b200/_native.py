@@ -19,6 +19,7 @@ FA_DTYPE_BF16 = 1
 FA_DTYPE_FP32 = 2
 
 FA_FLAG_FP32_TF32 = 1
+FA_FLAG_V_FP8_E5M2 = 2
 
 FA_OK = 0
 FA_ERR_INVALID_ARG = -1

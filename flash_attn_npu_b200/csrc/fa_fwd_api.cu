@@ -57,18 +57,25 @@ int device_ok(int dev) {
   return cache[dev] == 1;
 }
 
-int elt_bytes(int dtype) { return dtype == FA_DTYPE_FP32 ? 4 : 2; }
+// Element type of a tensor map: an FaDtype, or one byte (fp8 V).
+constexpr int kDtypeByte = 100;
+
+int elt_bytes(int dtype) {
+  return dtype == FA_DTYPE_FP32 ? 4 : (dtype == kDtypeByte ? 1 : 2);
+}
+
+bool v_fp8(const FaFwdArgs* a) { return (a->flags & FA_FLAG_V_FP8_E5M2) != 0; }
 
 bool head_dim_ok(int64_t d) { return d == 16 || d == 32 || d == 64 || d == 128 || d == 256; }
 
-fa::KernelInfo info_for(int64_t head_dim, int dtype, int block_n, int qt) {
+fa::KernelInfo info_for(int64_t head_dim, int dtype, int block_n, int qt, bool vf8 = false) {
   switch (head_dim) {
-    case 16: return fa::info_d16(dtype, block_n, qt);
-    case 32: return fa::info_d32(dtype, block_n, qt);
-    case 64: return fa::info_d64(dtype, block_n, qt);
-    case 128: return fa::info_d128(dtype, block_n, qt);
-    case 256: return fa::info_d256(dtype, block_n, qt);
-    default: return fa::KernelInfo{false, 0, 0, 0, 0, 0, 0};
+    case 16: return fa::info_d16(dtype, block_n, qt, vf8);
+    case 32: return fa::info_d32(dtype, block_n, qt, vf8);
+    case 64: return fa::info_d64(dtype, block_n, qt, vf8);
+    case 128: return fa::info_d128(dtype, block_n, qt, vf8);
+    case 256: return fa::info_d256(dtype, block_n, qt, vf8);
+    default: return fa::KernelInfo{false, 0, 0, 0, 0, 0, 0, 0, 0};
   }
 }
 
@@ -102,6 +109,7 @@ int encode_map(CUtensorMap* map, const void* ptr, int dtype, int64_t B, int64_t 
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   CUtensorMapDataType dt = dtype == FA_DTYPE_FP16   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                            : dtype == FA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                           : dtype == kDtypeByte    ? CU_TENSOR_MAP_DATA_TYPE_UINT8
                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   CUtensorMapSwizzle sw = atom32             ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
                           : swz_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
@@ -124,7 +132,11 @@ int validate(const FaFwdArgs* a) {
   if (!a->q || !a->k || !a->v || !a->o || !a->lse) return FA_ERR_INVALID_ARG;
   if (!std::isfinite(a->sm_scale)) return FA_ERR_INVALID_ARG;
   if (reinterpret_cast<uintptr_t>(a->lse) % 4 != 0) return FA_ERR_MISALIGNED;
-  if (a->flags & ~FA_FLAG_FP32_TF32) return FA_ERR_INVALID_ARG;
+  if (a->flags & ~(FA_FLAG_FP32_TF32 | FA_FLAG_V_FP8_E5M2)) return FA_ERR_INVALID_ARG;
+  if (v_fp8(a)) {
+    if (a->dtype == FA_DTYPE_FP32) return FA_ERR_UNSUPPORTED_DTYPE;
+    if (a->head_dim < 32) return FA_ERR_UNSUPPORTED_HEAD_DIM;
+  }
   return FA_OK;
 }
 
@@ -143,7 +155,7 @@ int resolve_tile(const FaFwdArgs* a, FaTileConfig* t) {
   }
   if (t->block_m != 128 && t->block_m != 256) return FA_ERR_UNSUPPORTED_TILE;
   if (t->block_n != 64 && t->block_n != 128) return FA_ERR_UNSUPPORTED_TILE;
-  const fa::KernelInfo ki = info_for(a->head_dim, a->dtype, t->block_n, t->block_m / 128);
+  const fa::KernelInfo ki = info_for(a->head_dim, a->dtype, t->block_n, t->block_m / 128, v_fp8(a));
   if (!ki.exists) return FA_ERR_UNSUPPORTED_TILE;
   const int smax = max_stages_for(ki);
   if (smax < 2) return FA_ERR_UNSUPPORTED_TILE;
@@ -156,8 +168,8 @@ int resolve_tile(const FaFwdArgs* a, FaTileConfig* t) {
 }  // namespace
 
 namespace fa {
-KernelInfo kernel_info(int head_dim, int dtype, int block_n, int qt) {
-  return info_for(head_dim, dtype, block_n, qt);
+KernelInfo kernel_info(int head_dim, int dtype, int block_n, int qt, bool vf8) {
+  return info_for(head_dim, dtype, block_n, qt, vf8);
 }
 }  // namespace fa
 
@@ -247,7 +259,8 @@ int fa_fwd_sm100(const FaFwdArgs* a, void* stream) {
   rc = resolve_tile(a, &t);
   if (rc != FA_OK) return rc;
   const int qt = t.block_m / 128;
-  const fa::KernelInfo ki = info_for(a->head_dim, a->dtype, t.block_n, qt);
+  const bool vf8 = v_fp8(a);
+  const fa::KernelInfo ki = info_for(a->head_dim, a->dtype, t.block_n, qt, vf8);
 
   fa::LaunchPlan lp;
   std::memset(&lp, 0, sizeof(lp));
@@ -257,8 +270,8 @@ int fa_fwd_sm100(const FaFwdArgs* a, void* stream) {
     rc = encode_map(&lp.tmK, a->k, a->dtype, B, H, S, D, a->k_stride, ki.box_cols, t.block_n,
                     ki.swz_bytes);
   if (rc == FA_OK)
-    rc = encode_map(&lp.tmV, a->v, a->dtype, B, H, S, D, a->v_stride, ki.box_cols, t.block_n,
-                    ki.swz_bytes, /*atom32=*/a->dtype == FA_DTYPE_FP32);
+    rc = encode_map(&lp.tmV, a->v, vf8 ? kDtypeByte : a->dtype, B, H, S, D, a->v_stride,
+                    ki.v_box_cols, t.block_n, ki.v_swz_bytes, /*atom32=*/a->dtype == FA_DTYPE_FP32);
   if (rc == FA_OK)
     rc = encode_map(&lp.tmO, a->o, a->dtype, B, H, S, D, a->o_stride, ki.box_cols, 128,
                     ki.swz_bytes);
@@ -279,6 +292,7 @@ int fa_fwd_sm100(const FaFwdArgs* a, void* stream) {
   lp.dtype = a->dtype;
   lp.block_n = t.block_n;
   lp.qt = qt;
+  lp.vf8 = vf8;
   lp.stream = static_cast<cudaStream_t>(stream);
 
   switch (D) {

@@ -8,6 +8,7 @@
 //   fp32 (tf32 MMA), D == 128       : (128,1), (64,1)
 //   fp32, D == 16: none (tf32 MN-major V needs 128-byte rows)
 //   fp32, D == 256: none (a 128-row fp32 query tile plus two K/V stages exceeds 227 KiB)
+//   fp8 V (fp16 / bf16 Q, K), D in {32, 64, 128} : (128,2), (128,1); D == 256 : (128,1), (64,1)
 #pragma once
 
 #include "fa_launch.h"
@@ -23,6 +24,17 @@ template <typename T>
 int dispatch_tile(const LaunchPlan& lp) {
   constexpr int D = FA_HEAD_DIM;
   constexpr bool kF32 = Elt<T>::kTf32;
+  if (lp.vf8) {
+    if constexpr (!kF32 && D >= 32) {
+      if (lp.block_n == 128 && lp.qt == 1) return launch_kernel<T, D, 128, 1, true>(lp);
+      if constexpr (D <= 128) {
+        if (lp.block_n == 128 && lp.qt == 2) return launch_kernel<T, D, 128, 2, true>(lp);
+      } else {
+        if (lp.block_n == 64 && lp.qt == 1) return launch_kernel<T, D, 64, 1, true>(lp);
+      }
+    }
+    return -5;
+  }
   if (lp.block_n == 128 && lp.qt == 1) return launch_kernel<T, D, 128, 1>(lp);
   if (lp.block_n == 64 && lp.qt == 1) return launch_kernel<T, D, 64, 1>(lp);
   if constexpr (!kF32 && D <= 128) {
@@ -36,9 +48,20 @@ int dispatch_tile(const LaunchPlan& lp) {
 }
 
 template <typename T>
-KernelInfo info_tile(int block_n, int qt) {
+KernelInfo info_tile(int block_n, int qt, bool vf8) {
   constexpr int D = FA_HEAD_DIM;
   constexpr bool kF32 = Elt<T>::kTf32;
+  if (vf8) {
+    if constexpr (!kF32 && D >= 32) {
+      if (block_n == 128 && qt == 1) return info_of<T, D, 128, 1, true>();
+      if constexpr (D <= 128) {
+        if (block_n == 128 && qt == 2) return info_of<T, D, 128, 2, true>();
+      } else {
+        if (block_n == 64 && qt == 1) return info_of<T, D, 64, 1, true>();
+      }
+    }
+    return KernelInfo{false, 0, 0, 0, 0, 0, 0, 0, 0};
+  }
   if (block_n == 128 && qt == 1) return info_of<T, D, 128, 1>();
   if (block_n == 64 && qt == 1) return info_of<T, D, 64, 1>();
   if constexpr (!kF32 && D <= 128) {
@@ -48,7 +71,7 @@ KernelInfo info_tile(int block_n, int qt) {
   if constexpr (kF32 && D <= 64) {
     if (block_n == 64 && qt == 2) return info_of<T, D, 64, 2>();
   }
-  return KernelInfo{false, 0, 0, 0, 0, 0, 0};
+  return KernelInfo{false, 0, 0, 0, 0, 0, 0, 0, 0};
 }
 
 }  // namespace
@@ -76,20 +99,20 @@ int FA_CAT(launch_d, FA_HEAD_DIM)(const LaunchPlan& lp) {
   }
 }
 
-KernelInfo FA_CAT(info_d, FA_HEAD_DIM)(int dtype, int block_n, int qt) {
+KernelInfo FA_CAT(info_d, FA_HEAD_DIM)(int dtype, int block_n, int qt, bool vf8) {
   switch (dtype) {
     case 0:
-      return info_tile<__half>(block_n, qt);
+      return info_tile<__half>(block_n, qt, vf8);
     case 1:
-      return info_tile<__nv_bfloat16>(block_n, qt);
+      return info_tile<__nv_bfloat16>(block_n, qt, vf8);
     case 2:
 #if FA_HEAD_DIM <= 128 && FA_HEAD_DIM >= 32
-      return info_tile<float>(block_n, qt);
+      return info_tile<float>(block_n, qt, vf8);
 #else
-      return KernelInfo{false, 0, 0, 0, 0, 0, 0};
+      return KernelInfo{false, 0, 0, 0, 0, 0, 0, 0, 0};
 #endif
     default:
-      return KernelInfo{false, 0, 0, 0, 0, 0, 0};
+      return KernelInfo{false, 0, 0, 0, 0, 0, 0, 0, 0};
   }
 }
 

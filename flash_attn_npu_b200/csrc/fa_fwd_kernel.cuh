@@ -39,6 +39,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <type_traits>
 
 #include "sm100_ptx.cuh"
 
@@ -86,9 +87,18 @@ struct Elt<float> {
   static constexpr uint32_t kFmt = 2;
   static constexpr bool kTf32 = true;
 };
+// float8 e5m2: the V operand (and P) of the fp8-V variant; kind::f8f6f4 format code 1.
+struct E5M2 {};
+template <>
+struct Elt<E5M2> {
+  static constexpr int kBytes = 1;
+  static constexpr uint32_t kFmt = 1;
+  static constexpr bool kTf32 = false;
+};
 
-// Compile-time geometry of one kernel instantiation.
-template <typename T, int D, int BN, int QT>
+// Compile-time geometry of one kernel instantiation.  VF8: V (and so P) is float8 e5m2 while
+// Q, K and O stay T.
+template <typename T, int D, int BN, int QT, bool VF8 = false>
 struct Geo {
   static constexpr int EB = Elt<T>::kBytes;
   static constexpr int ROW_BYTES = D * EB;                        // one row of Q/K/V/O
@@ -102,7 +112,17 @@ struct Geo {
   static constexpr int KV_TILE_BYTES = BN * ROW_BYTES;
   static constexpr int KSTEPS_PER_BLK = SWZ / 32;  // MMA K is always 32 bytes
   static constexpr int MMA_K = 32 / EB;            // 16 (f16/bf16) or 8 (tf32)
-  static constexpr int P_COLS = BN * EB / 4;       // TMEM columns holding P
+  // P and V share one element type: T, or e5m2 for the fp8-V variant.
+  using PT = typename std::conditional<VF8, E5M2, T>::type;
+  static constexpr int VEB = Elt<PT>::kBytes;
+  static constexpr int V_ROW_BYTES = D * VEB;
+  static constexpr int V_SWZ = VF8 ? (V_ROW_BYTES >= 128 ? 128 : V_ROW_BYTES) : SWZ;
+  static constexpr int V_BLK_COLS = V_SWZ / VEB;   // TMA box inner extent of V
+  static constexpr int V_NBLK = V_ROW_BYTES / V_SWZ;
+  static constexpr int V_BLK_BYTES = BN * V_SWZ;
+  static constexpr int V_TILE_BYTES = BN * V_ROW_BYTES;
+  static constexpr int PV_K = 32 / VEB;            // keys per P.V MMA (32 bytes of K)
+  static constexpr int P_COLS = BN * VEB / 4;      // TMEM columns holding P
   static constexpr int TMEM_S = 0;
   static constexpr int TMEM_O = QT * BN;
   static constexpr int TMEM_USED = QT * (BN + D);
@@ -121,10 +141,11 @@ struct Geo {
   static constexpr uint32_t LAYOUT = SWZ == 128 ? 2u : (SWZ == 64 ? 4u : 6u);
   // V is the MN-major operand of P.V.  For tf32 that operand needs the 32-byte-atom 128B
   // swizzle (descriptor code 1, 4-row K groups; TMA CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B).
-  static constexpr uint32_t V_LAYOUT = Elt<T>::kTf32 ? 1u : LAYOUT;
-  static constexpr int V_SBO = Elt<T>::kTf32 ? 4 * SWZ : 8 * SWZ;
+  static constexpr uint32_t V_LAYOUT =
+      Elt<T>::kTf32 ? 1u : (V_SWZ == 128 ? 2u : (V_SWZ == 64 ? 4u : 6u));
+  static constexpr int V_SBO = Elt<T>::kTf32 ? 4 * SWZ : 8 * V_SWZ;
   static constexpr uint32_t IDESC_S = make_idesc(Elt<T>::kFmt, false, 128, BN);
-  static constexpr uint32_t IDESC_O = make_idesc(Elt<T>::kFmt, true, 128, D);
+  static constexpr uint32_t IDESC_O = make_idesc(Elt<PT>::kFmt, true, 128, D);
   // Shared memory: [Q tiles][K/V ring][barriers]; +1024 for base alignment.
   static constexpr int BAR_BYTES = 256;
   static constexpr int smem_bytes(int stages) {
@@ -137,6 +158,8 @@ struct Geo {
   static_assert(ROW_BYTES % SWZ == 0, "row must be whole swizzle spans");
   static_assert(!Elt<T>::kTf32 || SWZ == 128, "tf32 needs rows of >= 128 bytes (head_dim >= 32)");
   static_assert(Q_BLK_BYTES % 1024 == 0 && KV_BLK_BYTES % 1024 == 0, "1 KiB tile alignment");
+  static_assert(!VF8 || (!Elt<T>::kTf32 && V_SWZ >= 32 && V_BLK_BYTES % 1024 == 0),
+                "fp8 V: 16-bit Q/K and rows of at least 32 bytes");
 };
 
 // Physical byte offset of logical byte `off` inside a TMA-swizzled region with span SWZ.
@@ -241,7 +264,7 @@ template <typename T, int BN, bool WITH_MAX>
 __device__ __forceinline__ float exp2_row_store(const float* s, float sl2, float neg_m, uint32_t tP,
                                                 float* mx) {
   constexpr int HALF = BN / 2;
-  constexpr int PW = Elt<T>::kTf32 ? HALF : HALF / 2;  // 32-bit TMEM words per half row
+  constexpr int PW = HALF * Elt<T>::kBytes / 4;  // 32-bit TMEM words per half row
   const float2 sc = make_float2(sl2, sl2);
   const float2 nm = make_float2(neg_m, neg_m);
   float2 acc[4];
@@ -255,6 +278,7 @@ __device__ __forceinline__ float exp2_row_store(const float* s, float sl2, float
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     uint32_t pk[PW];
+    float2 pend = make_float2(0.f, 0.f);
 #pragma unroll
     for (int k = h * HALF; k < (h + 1) * HALF; k += 2) {
       const float2 x = ffma2(make_float2(s[k], s[k + 1]), sc, nm);
@@ -271,6 +295,12 @@ __device__ __forceinline__ float exp2_row_store(const float* s, float sl2, float
       if constexpr (Elt<T>::kTf32) {
         pk[2 * w] = __float_as_uint(pr.x);
         pk[2 * w + 1] = __float_as_uint(pr.y);
+      } else if constexpr (Elt<T>::kBytes == 1) {
+        // four e5m2 per word: the even pair is held until the odd pair completes the word
+        if (w & 1)
+          pk[w >> 1] = pack4_e5m2(pend.x, pend.y, pr.x, pr.y);
+        else
+          pend = pr;
       } else {
         pk[w] = pack2(pr.x, pr.y, static_cast<T*>(nullptr));
       }
@@ -279,8 +309,10 @@ __device__ __forceinline__ float exp2_row_store(const float* s, float sl2, float
     for (int w = 0; w < PW; w += 32) {
       if constexpr (PW >= 32)
         tmem_st32(tP + h * PW + w, pk + w);
-      else
+      else if constexpr (PW >= 16)
         tmem_st16(tP + h * PW + w, pk + w);
+      else
+        tmem_st8(tP + h * PW + w, pk + w);
     }
   }
   if constexpr (WITH_MAX)
@@ -289,13 +321,14 @@ __device__ __forceinline__ float exp2_row_store(const float* s, float sl2, float
   return a.x + a.y;
 }
 
-template <typename T, int D, int BN, int QT>
-__global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
+template <typename T, int D, int BN, int QT, bool VF8 = false>
+__global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
     fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV,
                         const __grid_constant__ CUtensorMap tmO, const FaParams p) {
-  using G = Geo<T, D, BN, QT>;
+  using G = Geo<T, D, BN, QT, VF8>;
+  using PT = typename G::PT;  // element type of P and V
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -406,13 +439,21 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
               break;
             }
             const uint32_t fbar = smem_u32(&sh->full[slot]);
-            mbar_arrive_expect_tx(fbar, G::KV_TILE_BYTES);
-            const CUtensorMap* map = kv == 0 ? &tmK : &tmV;
             uint8_t* dst = kv_smem + slot * G::KV_TILE_BYTES;
+            if (kv == 0) {
+              mbar_arrive_expect_tx(fbar, G::KV_TILE_BYTES);
 #pragma unroll
-            for (int c = 0; c < G::NBLK; ++c)
-              tma_load_4d(smem_u32(dst + c * G::KV_BLK_BYTES), map, fbar, c * G::BLK_COLS, j * BN,
-                          hi, bi);
+              for (int c = 0; c < G::NBLK; ++c)
+                tma_load_4d(smem_u32(dst + c * G::KV_BLK_BYTES), &tmK, fbar, c * G::BLK_COLS,
+                            j * BN, hi, bi);
+            } else {
+              // V may be narrower than K (fp8); it starts at the slot's base either way.
+              mbar_arrive_expect_tx(fbar, G::V_TILE_BYTES);
+#pragma unroll
+              for (int c = 0; c < G::V_NBLK; ++c)
+                tma_load_4d(smem_u32(dst + c * G::V_BLK_BYTES), &tmV, fbar, c * G::V_BLK_COLS,
+                            j * BN, hi, bi);
+            }
             ++issued;
             if (++slot == stages) {
               slot = 0;
@@ -448,7 +489,7 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
       const uint64_t q_desc = make_smem_desc(smem_u32(q_smem), 16, 8 * G::SWZ, G::LAYOUT);
       const uint64_t k_desc = make_smem_desc(smem_u32(kv_smem), 16, 8 * G::SWZ, G::LAYOUT);
       const uint64_t v_desc =
-          make_smem_desc(smem_u32(kv_smem), G::KV_BLK_BYTES, G::V_SBO, G::V_LAYOUT);
+          make_smem_desc(smem_u32(kv_smem), G::V_BLK_BYTES, G::V_SBO, G::V_LAYOUT);
       constexpr uint32_t kSlotStep = G::KV_TILE_BYTES >> 4;
       const uint32_t full0 = smem_u32(&sh->full[0]);
       const uint32_t empty0 = smem_u32(&sh->empty[0]);
@@ -477,11 +518,13 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
         const uint32_t d = tmem + G::TMEM_O + i * D;
         const uint32_t a = tmem + G::TMEM_S + i * BN;
 #pragma unroll
-        for (int kk = 0; kk < BN / G::MMA_K; ++kk) {
-          // MMA_K keys = MMA_K rows of V; each TMEM column of P holds 4 bytes
-          const uint64_t bd = b0 + static_cast<uint64_t>((kk * G::MMA_K * G::SWZ) >> 4);
-          const uint32_t acol = static_cast<uint32_t>(kk * G::MMA_K * G::EB / 4);
-          if constexpr (Elt<T>::kTf32)
+        for (int kk = 0; kk < BN / G::PV_K; ++kk) {
+          // PV_K keys = PV_K rows of V; each TMEM column of P holds 4 bytes
+          const uint64_t bd = b0 + static_cast<uint64_t>((kk * G::PV_K * G::V_SWZ) >> 4);
+          const uint32_t acol = static_cast<uint32_t>(kk * G::PV_K * G::VEB / 4);
+          if constexpr (VF8)
+            mma_f8_ts(d, a + acol, bd, G::IDESC_O, kk > 0 ? 1u : acc0);
+          else if constexpr (Elt<T>::kTf32)
             mma_tf32_ts(d, a + acol, bd, G::IDESC_O, kk > 0 ? 1u : acc0);
           else
             mma_f16_ts(d, a + acol, bd, G::IDESC_O, kk > 0 ? 1u : acc0);
@@ -625,7 +668,7 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
         // that row takes the new base, O is rescaled, and the warp recomputes P.
         float mx;
         const float base = (m_used == -INFINITY) ? 0.f : -m_used;
-        float lt = exp2_row_store<T, BN, true>(s, sl2, base, tS, &mx);
+        float lt = exp2_row_store<PT, BN, true>(s, sl2, base, tS, &mx);
         const float m_tile = mx * sl2;
         const bool need = m_tile > m_used + RESCALE_LOG2;
         if (__any_sync(0xffffffffu, need)) {
@@ -637,7 +680,7 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
           }
           rescale_o(alpha);
           tmem_wait_st();  // the first pass's P stores land before they are overwritten
-          lt = exp2_row_store<T, BN, false>(s, sl2, -m_used, tS, nullptr);
+          lt = exp2_row_store<PT, BN, false>(s, sl2, -m_used, tS, nullptr);
         }
         l += lt;
       } else {
@@ -675,7 +718,7 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
         // p = 2^(s*scale_log2 - m_used); masked columns -> 0
         const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
         if (fast) {
-          l += exp2_row_store<T, BN, false>(s, sl2, neg_m, tS, nullptr);  // also writes P
+          l += exp2_row_store<PT, BN, false>(s, sl2, neg_m, tS, nullptr);  // also writes P
         } else {
           float l8[8];
 #pragma unroll
@@ -692,6 +735,17 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT>::NUM_THREADS, 1)
 #pragma unroll
             for (int c = 0; c < BN / 32; ++c)
               tmem_st32(tS + c * 32, reinterpret_cast<const uint32_t*>(s) + c * 32);
+          } else if constexpr (VF8) {
+            uint32_t pk[BN / 4];
+#pragma unroll
+            for (int k = 0; k < BN / 4; ++k)
+              pk[k] = pack4_e5m2(s[4 * k], s[4 * k + 1], s[4 * k + 2], s[4 * k + 3]);
+            if constexpr (BN / 4 >= 32) {
+#pragma unroll
+              for (int c = 0; c < BN / 128; ++c) tmem_st32(tS + c * 32, pk + c * 32);
+            } else {
+              tmem_st16(tS, pk);
+            }
           } else {
             uint32_t pk[BN / 2];
 #pragma unroll

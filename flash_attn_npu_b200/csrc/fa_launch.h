@@ -16,6 +16,7 @@ struct LaunchPlan {
   int dtype;    // FaDtype
   int block_n;  // 64 / 128
   int qt;       // query tiles per CTA (block_m / 128)
+  bool vf8;     // V (and P) in float8 e5m2
   int64_t grid;
   cudaStream_t stream;
 };
@@ -29,14 +30,16 @@ struct KernelInfo {
   int kv_tile_bytes;  // one BLOCK_N-row K or V tile
   int threads;
   int smem_fixed;     // bytes besides the K/V ring
+  int v_swz_bytes;    // swizzle span of V tiles (differs from the others for fp8 V)
+  int v_box_cols;     // TMA box inner extent of V (elements)
 };
 
-KernelInfo kernel_info(int head_dim, int dtype, int block_n, int qt);
-KernelInfo info_d16(int dtype, int block_n, int qt);
-KernelInfo info_d32(int dtype, int block_n, int qt);
-KernelInfo info_d64(int dtype, int block_n, int qt);
-KernelInfo info_d128(int dtype, int block_n, int qt);
-KernelInfo info_d256(int dtype, int block_n, int qt);
+KernelInfo kernel_info(int head_dim, int dtype, int block_n, int qt, bool vf8);
+KernelInfo info_d16(int dtype, int block_n, int qt, bool vf8);
+KernelInfo info_d32(int dtype, int block_n, int qt, bool vf8);
+KernelInfo info_d64(int dtype, int block_n, int qt, bool vf8);
+KernelInfo info_d128(int dtype, int block_n, int qt, bool vf8);
+KernelInfo info_d256(int dtype, int block_n, int qt, bool vf8);
 
 int launch_d16(const LaunchPlan& lp);
 int launch_d32(const LaunchPlan& lp);
@@ -45,10 +48,10 @@ int launch_d128(const LaunchPlan& lp);
 int launch_d256(const LaunchPlan& lp);
 
 // Launch one instantiation; returns 0 or FA_ERR_LAUNCH (-7) / FA_ERR_UNSUPPORTED_TILE (-5).
-template <typename T, int D, int BN, int QT>
+template <typename T, int D, int BN, int QT, bool VF8 = false>
 int launch_kernel(const LaunchPlan& lp) {
-  using G = Geo<T, D, BN, QT>;
-  auto kern = fa_fwd_sm100_kernel<T, D, BN, QT>;
+  using G = Geo<T, D, BN, QT, VF8>;
+  auto kern = fa_fwd_sm100_kernel<T, D, BN, QT, VF8>;
   const int smem = G::smem_bytes(lp.params.stages);
   if constexpr (QT == 2) {
     // setmaxnreg redistributes exactly the launch allocation; refuse to launch a build whose
@@ -74,12 +77,12 @@ int launch_kernel(const LaunchPlan& lp) {
   return cudaGetLastError() == cudaSuccess ? 0 : -7;
 }
 
-template <typename T, int D, int BN, int QT>
+template <typename T, int D, int BN, int QT, bool VF8 = false>
 constexpr KernelInfo info_of() {
-  using G = Geo<T, D, BN, QT>;
+  using G = Geo<T, D, BN, QT, VF8>;
   return KernelInfo{true,           G::SWZ,         G::BLK_COLS,
                     G::Q_TILE_BYTES, G::KV_TILE_BYTES, G::NUM_THREADS,
-                    G::smem_bytes(0)};
+                    G::smem_bytes(0), G::V_SWZ,      G::V_BLK_COLS};
 }
 
 }  // namespace fa

@@ -184,6 +184,29 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// D (+)= A B with 8-bit floating-point operands (A in TMEM): kind::f8f6f4, f32 accumulator.
+__device__ __forceinline__ void mma_f8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Rounds four floats to float8 e5m2 (round to nearest even, saturating to the largest finite
+// value) and packs them into one 32-bit word, `a` in the lowest byte.
+__device__ __forceinline__ uint32_t pack4_e5m2(float a, float b, float c, float d) {
+  uint32_t lo, hi;
+  // cvt.rn.satfinite.e5m2x2.f32 d, x, y puts x in the upper byte of the 16-bit result.
+  asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e5m2x2.f32 t, %2, %1;\n\tcvt.u32.u16 %0, t;\n\t}"
+      : "=r"(lo) : "f"(a), "f"(b));
+  asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e5m2x2.f32 t, %2, %1;\n\tcvt.u32.u16 %0, t;\n\t}"
+      : "=r"(hi) : "f"(c), "f"(d));
+  return lo | (hi << 16);
+}
+
 // Arrive once on `bar` when every tcgen05 async op issued so far by this thread has completed.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile(
@@ -246,6 +269,12 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
       "r"(r[15]));
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]));
 }
 
 // ------------------------------------------------------------ descriptors

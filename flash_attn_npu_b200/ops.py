@@ -29,6 +29,15 @@ def dtype_code(dtype: torch.dtype) -> int:
         raise ValueError(f"unsupported dtype {dtype}; expected float16, bfloat16 or float32")
 
 
+# V may be float8 e5m2 with fp16 / bf16 q and k: the reference's fp8_v mode
+# (flash_attention_forward.py:704, :996 -- P is rounded to float8e5 before P.V).
+V_FP8_DTYPE = torch.float8_e5m2
+
+
+def is_v_fp8(q: torch.Tensor, v: torch.Tensor) -> bool:
+    return v.dtype == V_FP8_DTYPE and q.dtype in (torch.float16, torch.bfloat16)
+
+
 def validate_inputs(q, k, v) -> None:
     """Reference `_validate_inputs` (flash_attention_forward.py:1114-1122) plus the CUDA rules."""
     if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
@@ -39,8 +48,11 @@ def validate_inputs(q, k, v) -> None:
         raise ValueError("q, k, v must be on the same device")
     if q.shape[-1] not in set(HEAD_DIMS):
         raise ValueError("HEAD_DIM must be one of {16, 32, 64, 128, 256}")
-    if q.dtype != k.dtype or q.dtype != v.dtype:
-        raise ValueError("q, k, v must have the same dtype")
+    if q.dtype != k.dtype or (q.dtype != v.dtype and not is_v_fp8(q, v)):
+        raise ValueError("q, k, v must have the same dtype (or v float8_e5m2 with float16/"
+                         "bfloat16 q, k)")
+    if is_v_fp8(q, v) and q.shape[-1] < 32:
+        raise ValueError("a float8_e5m2 v needs HEAD_DIM >= 32")
     dtype_code(q.dtype)
     if q.device.type != "cuda":
         raise ValueError(f"q, k, v must be CUDA tensors on an sm_100 device (got {q.device})")
@@ -74,6 +86,8 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_
     `status`, if given, is a device int32 tensor of one element that must be zero; a pipeline
     timeout inside the kernel writes a negative code there.  float32 inputs run in fp32 on the
     CUDA cores unless `fp32_tf32` selects the (faster, TF32-rounded) tensor-core kernel.
+    A float8_e5m2 `v` with float16/bfloat16 `q`, `k` runs the fp8-V kernel (P rounded to e5m2,
+    P.V on the fp8 tensor cores); `out` has q's dtype.
     """
     validate_inputs(q, k, v)
     z, h, n_ctx, head_dim = q.shape
@@ -106,7 +120,8 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_
         block_m=block_m, block_n=block_n, num_stages=num_stages,
         persistent_ctas=persistent_ctas,
         status_ptr=(status.data_ptr() if status is not None else None),
-        flags=_native.FA_FLAG_FP32_TF32 if fp32_tf32 else 0)
+        flags=((_native.FA_FLAG_FP32_TF32 if fp32_tf32 else 0)
+               | (_native.FA_FLAG_V_FP8_E5M2 if is_v_fp8(q, v) else 0)))
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
         try:

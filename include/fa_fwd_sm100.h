@@ -41,8 +41,12 @@ extern "C" {
  * FA_FLAG_FP32_TF32 (faster; TF32 rounding moves the logsumexp by ~1e-3). */
 enum FaDtype { FA_DTYPE_FP16 = 0, FA_DTYPE_BF16 = 1, FA_DTYPE_FP32 = 2 };
 
-/* FaFwdArgs.flags bits. */
-enum FaFlags { FA_FLAG_FP32_TF32 = 1 };
+/* FaFwdArgs.flags bits.
+ * FA_FLAG_V_FP8_E5M2: `v` holds float8 e5m2 values (one byte per element, strides in elements)
+ * while `dtype` (fp16 or bf16, head_dim >= 32) describes q, k and o; P is rounded to e5m2 and
+ * P.V runs on the fp8 tensor-core path.  Replaces the reference's fp8_v mode
+ * (flash_attention_forward.py:704, :996: taken when V is float8e5). */
+enum FaFlags { FA_FLAG_FP32_TF32 = 1, FA_FLAG_V_FP8_E5M2 = 2 };
 
 /* Return codes. */
 enum FaStatus {

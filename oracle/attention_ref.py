@@ -88,3 +88,70 @@ def attention_ref_numpy(q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: boo
     out = np.matmul(e / l, va)
     lse = (m + np.log(l))[..., 0]
     return out, lse
+
+
+# ----------------------------------------------------------------------------- fp8 V
+# The reference's fp8_v mode (flash_attention_forward.py:704 and :737, selected at :996 / :1017
+# when V is float8e5): Q and K stay 16-bit, P is rounded to float8 e5m2 before the P.V dot, the
+# running sum l keeps the unrounded fp32 p.  Two restatements, both on CPU in fp32:
+#   - attention_ref_fp8v_online: the reference's stable online softmax (:698-724) over key
+#     blocks of `block_n` -- m_ij = max(m_i, rowmax), p = exp(qk - m_ij), alpha = exp(m_i - m_ij),
+#     l = l*alpha + sum(p), acc = acc*alpha + fp8(p) @ v -- so P is rounded at the running max;
+#   - attention_kernel_order_fp8v: the same product with the exponent base the sm_100a kernel
+#     uses (base moves only when a block's max passes it by more than 8 in log2 units), so P is
+#     rounded at exactly the values the kernel rounds; it pins the kernel's fp8 rounding, while
+#     the online form bounds how far two valid orders of the same fp8 product can differ.
+
+def _masked_scores(q, k, causal, sm_scale):
+    s = (q.float() @ k.float().transpose(-1, -2)) * sm_scale
+    if causal:
+        n = s.shape[-1]
+        s = s.masked_fill(torch.triu(torch.ones(n, n, dtype=torch.bool), diagonal=1), float("-inf"))
+    return s
+
+
+def attention_ref_fp8v_online(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool,
+                              sm_scale: float, block_n: int = 128):
+    """Reference-order fp8-V attention on CPU; returns fp32 (out, lse)."""
+    s = _masked_scores(q, k, causal, sm_scale)
+    vf = v.float()
+    n = s.shape[-1]
+    m = torch.full(s.shape[:-1], float("-inf"))
+    l = torch.zeros(s.shape[:-1])
+    acc = torch.zeros(*s.shape[:-1], vf.shape[-1])
+    for j0 in range(0, n, block_n):
+        blk = s[..., j0:j0 + block_n]
+        m_new = torch.maximum(m, blk.amax(-1))
+        p = torch.exp(blk - m_new[..., None])
+        alpha = torch.exp(m - m_new)
+        l = l * alpha + p.sum(-1)
+        p8 = p.to(torch.float8_e5m2).float()
+        acc = acc * alpha[..., None] + p8 @ vf[..., j0:j0 + block_n, :]
+        m = m_new
+    return acc / l[..., None], m + torch.log(l)
+
+
+def attention_kernel_order_fp8v(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool,
+                                sm_scale: float, block_n: int = 128, threshold: float = 8.0):
+    """fp8-V attention with the sm_100a kernel's exponent bases; returns fp32 (out, lse)."""
+    x = _masked_scores(q, k, causal, sm_scale) * 1.4426950408889634  # log2 units
+    vf = v.float()
+    n = x.shape[-1]
+    m = torch.full(x.shape[:-1], float("-inf"))
+    l = torch.zeros(x.shape[:-1])
+    acc = torch.zeros(*x.shape[:-1], vf.shape[-1])
+    for j0 in range(0, n, block_n):
+        xb = x[..., j0:j0 + block_n]
+        mt = xb.amax(-1)
+        need = mt > m + threshold
+        m_new = torch.where(need, mt, m)
+        alpha = torch.where(need, torch.exp2(m - m_new), torch.ones_like(m))
+        l = l * alpha
+        acc = acc * alpha[..., None]
+        m = m_new
+        base = torch.where(torch.isinf(m), torch.zeros_like(m), m)
+        p = torch.exp2(xb - base[..., None])
+        l = l + p.sum(-1)
+        acc = acc + p.to(torch.float8_e5m2).float() @ vf[..., j0:j0 + block_n, :]
+    lse = (m + torch.log2(l)) * 0.6931471805599453
+    return acc / l[..., None], lse

@@ -220,3 +220,19 @@ def test_reference_evaluator_runs_through_the_shim(shim, monkeypatch):
     fallback = ev._reference_attention(None, q, k, v, 2, True, 0.5)
     assert (base - fallback).abs().max().item() < 1e-5
     assert tuple(ev.PERFORMANCE_CASES) == tuple(tuner.DEFAULT_SHAPES)
+
+
+def test_validate_inputs_fp8_v_rules():
+    """A float8_e5m2 v is accepted with 16-bit q/k (the reference's fp8_v mode); the CPU tensors
+    then fail only the device rule.  fp32 q/k or head_dim < 32 with an fp8 v are refused."""
+    from flash_attn_npu_b200 import ops
+    q = torch.zeros(1, 1, 8, 64, dtype=torch.bfloat16)
+    v8 = torch.zeros(1, 1, 8, 64).to(torch.float8_e5m2)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.validate_inputs(q, q, v8)
+    with pytest.raises(ValueError, match="same dtype"):
+        ops.validate_inputs(q.float(), q.float(), v8)
+    q16 = torch.zeros(1, 1, 8, 16, dtype=torch.float16)
+    with pytest.raises(ValueError, match="HEAD_DIM >= 32"):
+        ops.validate_inputs(q16, q16, torch.zeros(1, 1, 8, 16).to(torch.float8_e5m2))
+    assert ops.is_v_fp8(q, v8) and not ops.is_v_fp8(q.float(), v8)

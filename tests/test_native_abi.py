@@ -128,3 +128,28 @@ def test_grid_size(native_lib):
     a = _args(seqlen=1000, block_m=128, block_n=64)
     assert _native.grid_size(a) == 8 * 6
     assert _native.grid_size(_args(head_dim=40)) == -1
+
+
+def test_fp8_v_flag_validation(native_lib):
+    """FA_FLAG_V_FP8_E5M2: 16-bit q/k only, head_dim >= 32; unknown flag bits are rejected."""
+    lib = _native.load()
+    fl = _native.FA_FLAG_V_FP8_E5M2
+    cases = [
+        (_args(dtype_code=2, flags=fl), _native.FA_ERR_UNSUPPORTED_DTYPE),
+        (_args(head_dim=16, q_stride=(3 * 100 * 16, 100 * 16, 16),
+               k_stride=(3 * 100 * 16, 100 * 16, 16), v_stride=(3 * 100 * 16, 100 * 16, 16),
+               o_stride=(3 * 100 * 16, 100 * 16, 16), flags=fl), _native.FA_ERR_UNSUPPORTED_HEAD_DIM),
+        (_args(flags=8), _native.FA_ERR_INVALID_ARG),
+    ]
+    for a, want in cases:
+        assert lib.fa_fwd_sm100(ctypes.byref(a), None) == want
+    # the default tile exists for every fp8-V head dim and both 16-bit types
+    for d in (32, 64, 128, 256):
+        for code in (0, 1):
+            a = _args(head_dim=d, dtype_code=code, flags=fl, q_stride=(3 * 100 * d, 100 * d, d),
+                      k_stride=(3 * 100 * d, 100 * d, d), v_stride=(3 * 100 * d, 100 * d, d),
+                      o_stride=(3 * 100 * d, 100 * d, d))
+            assert _native.grid_size(a) > 0, (d, code)
+    # tiles outside the fp8-V set are refused before any launch
+    a = _args(flags=fl, seqlen=1000, block_m=256, block_n=64)
+    assert _native.grid_size(a) == -1

@@ -107,3 +107,56 @@ def test_sliced_matches_full():
     so, sl = attention_ref_sliced(q, k, v, True, 0.25, slices=[(1, 2), (0, 0)])
     torch.testing.assert_close(so[(1, 2)], out[1, 2])
     torch.testing.assert_close(sl[(0, 0)], lse[0, 0])
+
+
+# ----------------------------------------------------------------------------- fp8 V oracle
+from oracle.attention_ref import attention_kernel_order_fp8v, attention_ref_fp8v_online  # noqa: E402
+
+
+def _fp8_inputs(S, D, seed, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(1, 2, S, D, generator=g).to(dtype)
+    k = torch.randn(1, 2, S, D, generator=g).to(dtype)
+    v = torch.randn(1, 2, S, D, generator=g).to(torch.float8_e5m2)
+    return q, k, v
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_fp8v_orders_agree_within_e5m2_rounding(causal):
+    """Both fp8-V restatements round P to e5m2 (2 mantissa bits); they differ from the exact
+    fp32 attention, and from each other, only by that rounding; the LSE is unaffected."""
+    q, k, v = _fp8_inputs(384, 64, 1)
+    ex_o, ex_l = attention_ref_torch(q, k, v.float(), causal, 0.125)
+    on_o, on_l = attention_ref_fp8v_online(q, k, v, causal, 0.125)
+    ko_o, ko_l = attention_kernel_order_fp8v(q, k, v, causal, 0.125)
+    for o in (on_o, ko_o):
+        err = (o - ex_o).abs()
+        assert err.mean().item() < 1e-2 and err.max().item() < 0.15
+        assert err.mean().item() > 1e-4  # the rounding is really applied
+    assert torch.allclose(on_l, ex_l, atol=1e-5) and torch.allclose(ko_l, ex_l, atol=1e-5)
+
+
+def test_fp8v_single_block_orders_coincide():
+    """With one key block both orders round P at the row maximum: identical up to exp vs exp2
+    (a rounding flip needs p within ~1e-7 of an e5m2 midpoint)."""
+    q, k, v = _fp8_inputs(96, 32, 2)
+    on_o, _ = attention_ref_fp8v_online(q, k, v, False, 0.2, block_n=128)
+    ko_o, _ = attention_kernel_order_fp8v(q, k, v, False, 0.2, block_n=128)
+    assert (on_o - ko_o).abs().max().item() < 1e-3
+
+
+def test_fp8v_kernel_order_moves_base_only_past_threshold():
+    """A later block whose max exceeds the base by at most 8 (log2 units) keeps the base, so its
+    p reach 2^8; past the threshold the base moves and O is rescaled -- either way the result
+    equals the exact attention when every p is exactly representable in e5m2."""
+    S, D = 256, 32
+    k = torch.zeros(1, 1, S, D)
+    q = torch.zeros(1, 1, 1, D)
+    q[..., 0] = 1.0
+    v = torch.randn(1, 1, S, D, generator=torch.Generator().manual_seed(3)).to(torch.float8_e5m2)
+    for jump in (4.0, 20.0):  # log2-unit jump of the second block's logits
+        kk = k.clone()
+        kk[..., 128:, 0] = jump / 1.4426950408889634
+        out, _ = attention_kernel_order_fp8v(q, kk, v, False, 1.0)
+        ref, _ = attention_ref_torch(q, kk, v.float(), False, 1.0)
+        assert torch.allclose(out, ref, atol=1e-5, rtol=1e-5), jump
