@@ -18,6 +18,7 @@ fallback: without the built library every call raises.
 import argparse
 import json
 import os
+import sys
 import time
 from pathlib import Path
 
@@ -196,10 +197,14 @@ def _time_ms(fn, warmup, iters):
 
 
 def profiling(z, h, n_ctx, head_dim, causal, *args, **kwargs):
-    """Time the kernel with CUDA events and write `result_dir/profile_summary.{json,txt}`.
+    """Time the kernel with CUDA events, collect hardware counters with ncu, and write
+    `result_dir/profile_summary.{json,txt}`.
 
-    Argument forms match the reference (:1218-1247).  Hardware counters come from `ncu`
-    (see flash_attn_npu_b200.ncu_profile), not from this in-process timer.
+    Argument forms match the reference (:1218-1247).  The counters replace the reference's
+    torch_npu AiC metric passes (:1262-1289): `flash_attn_npu_b200.ncu_profile` runs this
+    module's one-launch `tune` command under `ncu` (metric groups Timing, SpeedOfLight, Memory,
+    Pipes, Issue; only Timing for inputs over 2 GiB).  FA_PROFILE_NCU=0 skips that step; without
+    ncu on PATH the summary records why the counters are missing.
     """
     sm_scale_kw = kwargs.pop("sm_scale", None)
     if kwargs:
@@ -240,14 +245,37 @@ def profiling(z, h, n_ctx, head_dim, causal, *args, **kwargs):
         "tflops": flops / (median * 1e-3) / 1e12,
         "samples_ms": times,
     }
+    if os.environ.get("FA_PROFILE_NCU", "1") != "0":
+        summary["ncu"] = _ncu_counters(z, h, n_ctx, head_dim, causal, q, sm_scale)
     result_dir = Path.cwd() / RESULT_DIR_NAME
     result_dir.mkdir(parents=True, exist_ok=True)
     (result_dir / "profile_summary.json").write_text(json.dumps(summary, indent=2) + "\n")
-    (result_dir / "profile_summary.txt").write_text(
-        f"{PROFILE_OP_NAME} {summary['shape']} {summary['dtype']}: median {median:.3f} ms, "
-        f"{summary['tflops']:.1f} TFLOP/s\n")
+    lines = [f"{PROFILE_OP_NAME} {summary['shape']} {summary['dtype']}: median {median:.3f} ms, "
+             f"{summary['tflops']:.1f} TFLOP/s"]
+    for group, vals in summary.get("ncu", {}).get("groups", {}).items():
+        lines.append(f"[{group}] " + ", ".join(f"{m} = {v:g}" for m, v in vals.items()))
+    if "error" in summary.get("ncu", {}):
+        lines.append(f"[ncu] {summary['ncu']['error']}")
+    (result_dir / "profile_summary.txt").write_text("\n".join(lines) + "\n")
     print(f"median {median:.3f} ms, {summary['tflops']:.1f} TFLOP/s; results in {result_dir}")
     return summary
+
+
+def _ncu_counters(z, h, n_ctx, head_dim, causal, q, sm_scale):
+    """ncu metric groups for one launch of this configuration (in a child process)."""
+    from flash_attn_npu_b200 import ncu_profile as _ncu
+    in_bytes = 3 * q.numel() * q.element_size()
+    groups = (_ncu.METRIC_GROUPS if in_bytes <= _ncu.MAX_MULTIPASS_BYTES
+              else {g: _ncu.METRIC_GROUPS[g] for g in _ncu.SINGLE_PASS_GROUPS})
+    argv = [sys.executable, str(Path(__file__).resolve()), "tune", "--z", str(z), "--h", str(h),
+            "--n-ctx", str(n_ctx), "--head-dim", str(head_dim),
+            "--dtype", str(q.dtype).replace("torch.", ""), "--sm-scale", repr(float(sm_scale))]
+    if causal:
+        argv.append("--causal")
+    try:
+        return _ncu.profile(argv, groups)
+    except Exception as exc:  # the timing above stays valid without counters
+        return {"error": str(exc)}
 
 
 # ----------------------------------------------------------------------------- CLI

@@ -236,3 +236,21 @@ def test_validate_inputs_fp8_v_rules():
     with pytest.raises(ValueError, match="HEAD_DIM >= 32"):
         ops.validate_inputs(q16, q16, torch.zeros(1, 1, 8, 16).to(torch.float8_e5m2))
     assert ops.is_v_fp8(q, v8) and not ops.is_v_fp8(q.float(), v8)
+
+
+def test_ncu_raw_csv_parser_and_groups():
+    """`ncu --csv --page raw` output (header, units, one row per launch) -> metric groups."""
+    from flash_attn_npu_b200 import ncu_profile
+    text = ('==PROF== Connected to process\n'
+            '"ID","Kernel Name","gpu__time_duration.sum","dram__bytes_read.sum","launch__grid_size"\n'
+            '"","","nsecond","byte",""\n'
+            '"0","fa_fwd_sm100_kernel","1,234","5,000,000","148"\n')
+    rows = ncu_profile.parse_raw_csv(text)
+    assert rows[0]["gpu__time_duration.sum"] == 1234.0
+    assert rows[0]["dram__bytes_read.sum"] == 5e6
+    g = ncu_profile.group_summary(rows[0], {"Timing": ["gpu__time_duration.sum"],
+                                            "Memory": ["dram__bytes_read.sum", "missing"]})
+    assert g == {"Timing": {"gpu__time_duration.sum": 1234.0},
+                 "Memory": {"dram__bytes_read.sum": 5e6}}
+    assert ncu_profile.parse_raw_csv("no csv here") == []
+    assert set(ncu_profile.SINGLE_PASS_GROUPS) <= set(ncu_profile.METRIC_GROUPS)
