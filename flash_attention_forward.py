@@ -24,6 +24,7 @@ from pathlib import Path
 
 import torch
 
+from flash_attn_npu_b200 import host_stream as _host_stream
 from flash_attn_npu_b200 import ops as _ops
 from flash_attn_npu_b200 import tiling as _tiling
 
@@ -163,6 +164,25 @@ def attention(q, k, v, causal, sm_scale, BM=None, BN=None, return_lse=False):
     if return_lse:
         return out, lse
     return out
+
+
+def attention_host(q, k, v, causal, sm_scale, BM=None, BN=None, return_lse=False, device=None,
+                   out=None, lse=None):
+    """`attention` for host (CPU, ideally pinned) q, k, v: the (b, h) slices are streamed
+    through the GPU with the host copies overlapping the kernels; returns host tensors.  The
+    tile config is resolved for the full [Z, H, N_CTX, D] shape, as `_launch_kernel` does."""
+    _ops.validate_layout(q, k, v)
+    z, h, n_ctx, head_dim = q.shape
+    cfg, source = _resolve_config(z, h, n_ctx, head_dim, causal, q.dtype, BM, BN)
+    if _ops.is_v_fp8(q, v) and source != "override":
+        cfg = _tiling.TileConfig(0, 0, 0, cfg.persistent_ctas)
+    o, l = _host_stream.forward_host(q, k, v, bool(causal), float(sm_scale), device=device,
+                                     out=out, lse=lse, block_m=cfg.block_m,
+                                     block_n=cfg.block_n, num_stages=cfg.num_stages,
+                                     persistent_ctas=cfg.persistent_ctas)
+    if return_lse:
+        return o, l
+    return o
 
 
 # ----------------------------------------------------------------------------- profiling

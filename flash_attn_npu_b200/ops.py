@@ -40,6 +40,13 @@ def is_v_fp8(q: torch.Tensor, v: torch.Tensor) -> bool:
 
 def validate_inputs(q, k, v) -> None:
     """Reference `_validate_inputs` (flash_attention_forward.py:1114-1122) plus the CUDA rules."""
+    validate_layout(q, k, v)
+    if q.device.type != "cuda":
+        raise ValueError(f"q, k, v must be CUDA tensors on an sm_100 device (got {q.device})")
+
+
+def validate_layout(q, k, v) -> None:
+    """The shape, head-dim and dtype rules of `validate_inputs`, on tensors on any device."""
     if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
         raise ValueError("q, k, v must all be 4D tensors shaped [Z, H, N_CTX, HEAD_DIM]")
     if q.shape != k.shape or q.shape != v.shape:
@@ -54,8 +61,6 @@ def validate_inputs(q, k, v) -> None:
     if is_v_fp8(q, v) and q.shape[-1] < 32:
         raise ValueError("a float8_e5m2 v needs HEAD_DIM >= 32")
     dtype_code(q.dtype)
-    if q.device.type != "cuda":
-        raise ValueError(f"q, k, v must be CUDA tensors on an sm_100 device (got {q.device})")
 
 
 def _tma_ok(t: torch.Tensor) -> bool:
