@@ -52,6 +52,10 @@ namespace fa {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float RESCALE_LOG2 = 8.0f;
+// Every p = 2^(x - base) of a row is <= 2^RESCALE_LOG2 whenever the row's sum is; the bound
+// sits just below 256 so that an element at the limit (ex2.approx may round it to 256) still
+// sends the row through the exact max check.
+constexpr float P_SUM_BOUND = 255.0f;
 constexpr int kMaxStages = 8;
 constexpr int kStatusTimeout = -9;  // FA_ERR_DEVICE_TIMEOUT
 
@@ -257,12 +261,10 @@ __device__ __forceinline__ float row_max(const float* s) {
 // P = 2^(s*sl2 + neg_m) for an unmasked row, written to TMEM at tP in two halves: the store of
 // the first half is in flight while the second half is computed (the caller waits once; the
 // store reads its source registers asynchronously, so finer chunking would pin more of them).
-// Returns the row sum of the unrounded fp32 values; with WITH_MAX it also returns max(s) through
-// *mx, computed in the same pass (ALU work that overlaps the MUFU exponentials).  s is left
-// intact.  A fixed share of the element pairs can go through the FMA-pipe polynomial.
-template <typename T, int BN, bool WITH_MAX>
-__device__ __forceinline__ float exp2_row_store(const float* s, float sl2, float neg_m, uint32_t tP,
-                                                float* mx) {
+// Returns the row sum of the unrounded fp32 values.  s is left intact.  A fixed share of the
+// element pairs can go through the FMA-pipe polynomial.
+template <typename T, int BN>
+__device__ __forceinline__ float exp2_row_store(const float* s, float sl2, float neg_m, uint32_t tP) {
   constexpr int HALF = BN / 2;
   constexpr int PW = HALF * Elt<T>::kBytes / 4;  // 32-bit TMEM words per half row
   const float2 sc = make_float2(sl2, sl2);
@@ -270,11 +272,6 @@ __device__ __forceinline__ float exp2_row_store(const float* s, float sl2, float
   float2 acc[4];
 #pragma unroll
   for (int t = 0; t < 4; ++t) acc[t] = make_float2(0.f, 0.f);
-  float e[8];
-  if constexpr (WITH_MAX) {
-#pragma unroll
-    for (int t = 0; t < 8; ++t) e[t] = -INFINITY;
-  }
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     uint32_t pk[PW];
@@ -290,7 +287,6 @@ __device__ __forceinline__ float exp2_row_store(const float* s, float sl2, float
         pr.y = ex2_approx(x.y);
       }
       acc[(k >> 1) & 3] = fadd2(acc[(k >> 1) & 3], pr);
-      if constexpr (WITH_MAX) e[(k >> 1) & 7] = fmax3(e[(k >> 1) & 7], s[k], s[k + 1]);
       const int w = (k - h * HALF) >> 1;
       if constexpr (Elt<T>::kTf32) {
         pk[2 * w] = __float_as_uint(pr.x);
@@ -315,8 +311,6 @@ __device__ __forceinline__ float exp2_row_store(const float* s, float sl2, float
         tmem_st8(tP + h * PW + w, pk + w);
     }
   }
-  if constexpr (WITH_MAX)
-    *mx = fmax3(fmax3(e[0], e[1], e[2]), fmax3(e[3], e[4], e[5]), fmaxf(e[6], e[7]));
   const float2 a = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
   return a.x + a.y;
 }
@@ -663,24 +657,27 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
       };
 
       if (fast && j > 0) {
-        // Optimistic pass: exponentiate against the current base and take the row max in the
-        // same pass.  Exact unless some row's max moved past base + RESCALE_LOG2; then (rare)
-        // that row takes the new base, O is rescaled, and the warp recomputes P.
-        float mx;
+        // Optimistic pass: exponentiate against the current base.  The row max is only needed
+        // when the row sum exceeds P_SUM_BOUND (rare once the base has settled; a row whose
+        // max moved past base + RESCALE_LOG2 always does): then a row that needs it takes the
+        // new base, O is rescaled, and the warp recomputes P.  The decisions are those of a
+        // max taken every step.
         const float base = (m_used == -INFINITY) ? 0.f : -m_used;
-        float lt = exp2_row_store<PT, BN, true>(s, sl2, base, tS, &mx);
-        const float m_tile = mx * sl2;
-        const bool need = m_tile > m_used + RESCALE_LOG2;
-        if (__any_sync(0xffffffffu, need)) {
-          float alpha = 1.f;
-          if (need) {
-            alpha = ex2_approx(m_used - m_tile);  // m_used = -inf gives 0
-            l *= alpha;
-            m_used = m_tile;
+        float lt = exp2_row_store<PT, BN>(s, sl2, base, tS);
+        if (__any_sync(0xffffffffu, !(lt <= P_SUM_BOUND) || m_used == -INFINITY)) {
+          const float m_tile = row_max<BN>(s) * sl2;
+          const bool need = m_tile > m_used + RESCALE_LOG2;
+          if (__any_sync(0xffffffffu, need)) {
+            float alpha = 1.f;
+            if (need) {
+              alpha = ex2_approx(m_used - m_tile);  // m_used = -inf gives 0
+              l *= alpha;
+              m_used = m_tile;
+            }
+            rescale_o(alpha);
+            tmem_wait_st();  // the first pass's P stores land before they are overwritten
+            lt = exp2_row_store<PT, BN>(s, sl2, -m_used, tS);
           }
-          rescale_o(alpha);
-          tmem_wait_st();  // the first pass's P stores land before they are overwritten
-          lt = exp2_row_store<PT, BN, false>(s, sl2, -m_used, tS, nullptr);
         }
         l += lt;
       } else {
@@ -718,7 +715,7 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
         // p = 2^(s*scale_log2 - m_used); masked columns -> 0
         const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
         if (fast) {
-          l += exp2_row_store<PT, BN, false>(s, sl2, neg_m, tS, nullptr);  // also writes P
+          l += exp2_row_store<PT, BN>(s, sl2, neg_m, tS);  // also writes P
         } else {
           float l8[8];
 #pragma unroll
