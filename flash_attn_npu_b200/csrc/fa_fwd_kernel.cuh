@@ -556,20 +556,25 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < QT; ++i) {
           if (j >= n_kv[i]) continue;
+          // Every wait comes before the tile's MMAs: a wait or a branch between two MMA
+          // groups idles the tensor pipe (it holds little more than the MMA in flight), so
+          // P_i(j) V_j and the next Q_i K_{j+1}^T go out as one straight run.
+          const bool s_next = j + 1 < n_kv[i];
+          if (s_next && !k_ready) {
+            ok = wait_bar(sh, full0 + 8u * ks, kph, p.status);
+            if (!ok) break;
+            k_ready = true;
+          }
           ok = wait_bar(sh, smem_u32(&sh->p_full[i]), static_cast<uint32_t>(j & 1), p.status);
           if (!ok) break;
           tc_fence_after();
-          issue_pv(i, vs, j > 0 ? 1u : 0u);
-          if (j == n_kv[i] - 1) mma_commit(smem_u32(&sh->o_full[i]));
-          if (j + 1 < n_kv[i]) {
-            if (!k_ready) {
-              ok = wait_bar(sh, full0 + 8u * ks, kph, p.status);
-              if (!ok) break;
-              tc_fence_after();
-              k_ready = true;
-            }
+          if (s_next) {
+            issue_pv(i, vs, j > 0 ? 1u : 0u);
             issue_s(i, ks);
             mma_commit(smem_u32(&sh->s_full[i]));
+          } else {
+            issue_pv(i, vs, j > 0 ? 1u : 0u);
+            mma_commit(smem_u32(&sh->o_full[i]));
           }
         }
         if (!ok) break;
