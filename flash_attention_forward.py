@@ -40,11 +40,11 @@ PROFILE_OP_NAME = "fa_fwd_sm100_kernel"
 # (Z, H, N_CTX, HEAD_DIM, causal): (BLOCK_M, BLOCK_N, NUM_STAGES, PERSISTENT_CTAS)
 DEFAULT_TILING_PRESETS = {
     (128, 8, 1024, 128, True): (256, 128, 4, 0),
-    (128, 8, 1024, 256, True): (128, 128, 2, 0),
+    (128, 8, 1024, 256, True): (128, 64, 4, 0),
     (128, 8, 2048, 128, True): (256, 128, 4, 0),
     (128, 8, 2048, 256, False): (128, 128, 2, 0),
-    (128, 8, 4096, 128, False): (256, 128, 3, 0),
-    (128, 8, 8192, 64, False): (256, 128, 3, 0),
+    (128, 8, 4096, 128, False): (256, 128, 4, 0),
+    (128, 8, 8192, 64, False): (256, 128, 6, 0),
 }
 # END AUTO-TUNED DEFAULT TILING PRESETS
 
