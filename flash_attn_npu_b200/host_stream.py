@@ -30,9 +30,11 @@ _streams: dict[int, tuple] = {}
 
 
 def plan_chunks(n_slices: int, slice_bytes: int, target_bytes: int = TARGET_CHUNK_BYTES,
-                chunk_slices: int | None = None) -> list[tuple[int, int]]:
+                chunk_slices: int | None = None, tail_split: int = 4) -> list[tuple[int, int]]:
     """[start, stop) slice ranges: `chunk_slices` per chunk, or as many as fit `target_bytes`
-    (at least one), with the remainder in the last chunk."""
+    (at least one), with the remainder in the last chunk.  When there is more than one chunk
+    the last one is cut into `tail_split` smaller pieces: the last chunk's kernel and copy-out
+    are the only part of the pipeline no copy-in overlaps."""
     if n_slices <= 0:
         return []
     if chunk_slices is None:
@@ -40,7 +42,12 @@ def plan_chunks(n_slices: int, slice_bytes: int, target_bytes: int = TARGET_CHUN
     if chunk_slices <= 0:
         raise ValueError("chunk_slices must be positive")
     cs = min(chunk_slices, n_slices)
-    return [(s, min(s + cs, n_slices)) for s in range(0, n_slices, cs)]
+    chunks = [(s, min(s + cs, n_slices)) for s in range(0, n_slices, cs)]
+    if len(chunks) > 1 and tail_split > 1:
+        a, b = chunks.pop()
+        piece = max(1, -(-(b - a) // tail_split))
+        chunks += [(s, min(s + piece, b)) for s in range(a, b, piece)]
+    return chunks
 
 
 def _side_streams(device: torch.device):

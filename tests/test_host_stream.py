@@ -19,15 +19,22 @@ def test_plan_chunks_cover_every_slice_once(n, slice_bytes, target, cs):
     assert covered == list(range(n))
     sizes = [b - a for a, b in chunks]
     assert all(x > 0 for x in sizes)
-    assert all(x == sizes[0] for x in sizes[:-1]) and sizes[-1] <= sizes[0]
-    if cs is None:
-        assert sizes[0] == min(n, max(1, target // slice_bytes))
+    assert all(x >= y for x, y in zip(sizes, sizes[1:]))  # never grows: the tail is split finer
+    full = min(n, max(1, target // slice_bytes)) if cs is None else min(n, cs)
+    assert sizes[0] == full
+    n_full = -(-n // full)
+    if n_full > 1:  # the last uniform chunk became at most 4 pieces
+        assert all(x == full for x in sizes[:n_full - 1])
+        assert 1 <= len(sizes) - (n_full - 1) <= 4
     else:
-        assert sizes[0] == min(n, cs)
+        assert sizes == [n]
 
 
 def test_plan_chunks_edges():
     assert host_stream.plan_chunks(0, 100) == []
+    chunks = host_stream.plan_chunks(256, 6 << 20)  # 16-slice chunks, the last one in four
+    assert chunks[-5:] == [(224, 240), (240, 244), (244, 248), (248, 252), (252, 256)]
+    assert host_stream.plan_chunks(10, 1, 4, tail_split=1) == [(0, 4), (4, 8), (8, 10)]
     with pytest.raises(ValueError):
         host_stream.plan_chunks(4, 100, chunk_slices=0)
 
