@@ -631,7 +631,17 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
         lim = max(0, min(lim, BN));
       }
       const bool masked = tail || diag;
-      const bool fast = use_max && !masked;
+      // With a positive scale a masked step runs the unmasked routines on logits whose masked
+      // columns are set to -inf: 2^-inf = 0 and the row max ignores them.  (A zero scale
+      // would turn -inf into NaN, a negative one flips the extreme: those keep the
+      // per-element path below.)
+      const bool mask_inf = masked && sl2 > 0.f;
+      if (mask_inf) {
+#pragma unroll
+        for (int k = 0; k < BN; ++k)
+          if (k >= lim) s[k] = -INFINITY;
+      }
+      const bool fast = use_max && (!masked || mask_inf);
       const float fill = use_max ? -INFINITY : INFINITY;
 
       // O_i holds the sum over steps < j (S_i(j) completion implies P_i(j-1) V_{j-1} is done),
