@@ -13,8 +13,9 @@
 // CTA shape (one CTA per SM; TMEM and shared memory sized for that):
 //   QT query tiles of 128 rows for one (batch, head); BLOCK_M = 128 * QT.
 //   warp 0        : TMA producer (Q once, then K/V tiles into a ring of `stages` slots)
-//   warp 1        : TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2-3     : idle (keep the softmax warpgroups aligned to TMEM lane quarters)
+//   warp 1        : TMEM allocator + tcgen05.mma issuer (one thread; with QT == 2, tile 0's)
+//   warp 2        : QT == 2: tcgen05.mma issuer of tile 1 (the two issuers take turns)
+//   warps 2-3     : otherwise idle (keep the softmax warpgroups aligned to TMEM lane quarters)
 //   warps 4+4i..  : softmax warpgroup i (thread r owns query row r of tile i = TMEM lane r)
 // TMEM columns: S_i (fp32 logits, BN cols) at i*BN, then O_i (fp32, D cols) at QT*BN + i*D.
 // P_i (the probabilities, in the input dtype) is written back over the first columns of S_i
@@ -58,6 +59,13 @@ constexpr float RESCALE_LOG2 = 8.0f;
 constexpr float P_SUM_BOUND = 255.0f;
 constexpr int kMaxStages = 8;
 constexpr int kStatusTimeout = -9;  // FA_ERR_DEVICE_TIMEOUT
+
+// With two query tiles per CTA the MMAs are issued from two warps, one per tile, which take
+// turns through a pair of named barriers (see the MMA issuers in the kernel).  0 keeps the
+// single issuing thread.
+#ifndef FA_DUAL_ISSUE
+#define FA_DUAL_ISSUE 1
+#endif
 
 struct FaParams {
   int batch;
@@ -333,6 +341,9 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int stages = p.stages;
+  // Two issuing warps (QT == 2): every K/V slot is released by one arrival per issuer.
+  constexpr bool kDual = QT == 2 && FA_DUAL_ISSUE != 0;
+  constexpr uint32_t kIssuers = kDual ? 2u : 1u;
 
   // ---- tile coordinates (causal: longest q-blocks first; non-causal: q-blocks of one head
   //      adjacent so K/V stay in L2 -- the reference's two orders, :915-922)
@@ -368,7 +379,7 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(smem_u32(&sh->full[s]), 1);
-      mbar_init(smem_u32(&sh->empty[s]), 1);
+      mbar_init(smem_u32(&sh->empty[s]), kIssuers);
     }
     mbar_init(smem_u32(&sh->q_full), 1);
     for (int i = 0; i < 2; ++i) {
@@ -376,7 +387,7 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
       mbar_init(smem_u32(&sh->p_full[i]), 128);
       mbar_init(smem_u32(&sh->o_full[i]), 1);
     }
-    mbar_init(smem_u32(&sh->mma_done), 1);
+    mbar_init(smem_u32(&sh->mma_done), kIssuers);
     sh->abort_flag = 0u;
     fence_mbar_init();
   }
@@ -470,12 +481,10 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
         }
       }
     }
-  } else if (warp == 1) {
-    // ================================================================ MMA issuer
-    if (lane == 0 && n_max > 0) {
-      bool ok = wait_bar(sh, smem_u32(&sh->q_full), 0, p.status);
-      tc_fence_after();
-      // This single thread shares its SM sub-partition with two busy softmax warps, so its
+  } else if (warp == 1 || (kDual && warp == 2)) {
+    // ================================================================ MMA issuer(s)
+    {
+      // The issuing thread shares its SM sub-partition with two busy softmax warps, so its
       // instruction stream is kept minimal: descriptors are built once and their start-address
       // field (bits 0-13 = address >> 4) is advanced by adding byte offsets >> 4 (shared memory
       // stays below 256 KiB, so the field never carries into the next one); ring slots and
@@ -530,6 +539,95 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
           ph ^= 1u;
         }
       };
+
+      if constexpr (kDual) {
+        // Two issuers: warp 1 issues tile 0's MMAs, warp 2 tile 1's (lane 0 issues, the warp
+        // stays converged for the named barriers).  They take turns -- S_0(0), S_1(0), then per
+        // step j: P_0(j) V_j + Q_0 K_{j+1}^T, P_1(j) V_j + Q_1 K_{j+1}^T -- so the tensor pipe sees
+        // the single issuer's order, but each warp waits for its own operands (V_j, K_{j+1},
+        // P_i(j)) while the other warp's MMAs are going out, and picks up the turn with one
+        // named-barrier hand-off instead of a chain of mbarrier waits between two MMA runs.
+        // Turn passing: barrier kTok0 (tile 0 done -> tile 1 may issue), kTok1 (the reverse);
+        // bar.arrive by the passer, bar.sync by the taker.  Both warps run the same number of
+        // hand-offs whatever happens (an aborted wait only stops the issuing), so neither is
+        // left waiting on a named barrier.
+        // A K/V slot's empty barrier counts two arrivals: each tile that reads the slot commits
+        // once, and a tile that is the slot's only reader (the other tile has run out of keys,
+        // causal, or lies past the sequence end) commits twice.  Every commit follows MMAs that
+        // read the slot, so no arrival can land in the slot's previous phase.
+        constexpr uint32_t kTok0 = 3, kTok1 = 4;
+        const int ti = warp - 1;
+        const bool lead = lane == 0;
+        auto pass_turn = [&]() {
+          __syncwarp();
+          named_barrier_arrive(ti == 0 ? kTok0 : kTok1, 64);
+        };
+        auto take_turn = [&]() {
+          __syncwarp();
+          named_barrier_sync(ti == 0 ? kTok1 : kTok0, 64);
+        };
+        auto wait_all = [&](uint32_t bar, uint32_t parity) {
+          return __all_sync(0xffffffffu, wait_bar(sh, bar, parity, p.status));
+        };
+        if (n_max > 0) {
+          const int mine = ti == 0 ? n_kv[0] : n_kv[QT - 1];
+          const int other = ti == 0 ? n_kv[QT - 1] : n_kv[0];
+          bool ok = wait_all(smem_u32(&sh->q_full), 0);
+          if (ok) ok = wait_all(full0, 0);  // K_0
+          tc_fence_after();
+          if (ti == 1) take_turn();
+          if (ok && lead && mine > 0) {
+            issue_s(ti, 0);
+            mma_commit(smem_u32(&sh->s_full[ti]));
+            mma_commit(empty0);
+            if (other == 0) mma_commit(empty0);
+          }
+          pass_turn();
+          int vs = 0;
+          uint32_t vph = 0;
+          advance(vs, vph);  // V_0
+          for (int j = 0; j < n_max; ++j) {
+            int ks = vs;
+            uint32_t kph = vph;
+            advance(ks, kph);  // K_{j+1}
+            const bool act = j < mine;          // P_i(j) V_j
+            const bool s_next = j + 1 < mine;   // Q_i K_{j+1}^T
+            if (ok && act) ok = wait_all(full0 + 8u * vs, vph);
+            if (ok && s_next) ok = wait_all(full0 + 8u * ks, kph);
+            if (ok && act) ok = wait_all(smem_u32(&sh->p_full[ti]), static_cast<uint32_t>(j & 1));
+            tc_fence_after();
+            take_turn();
+            if (ok && act && lead) {
+              issue_pv(ti, vs, j > 0 ? 1u : 0u);
+              if (s_next) {
+                issue_s(ti, ks);
+                mma_commit(smem_u32(&sh->s_full[ti]));
+              } else {
+                mma_commit(smem_u32(&sh->o_full[ti]));
+              }
+              mma_commit(empty0 + 8u * vs);
+              if (j >= other) mma_commit(empty0 + 8u * vs);
+              if (s_next) {
+                mma_commit(empty0 + 8u * ks);
+                if (j + 1 >= other) mma_commit(empty0 + 8u * ks);
+              }
+            }
+            pass_turn();
+            vs = ks;
+            vph = kph;
+            advance(vs, vph);  // V_{j+1}
+          }
+          if (ti == 0) take_turn();  // tile 1's last hand-off
+          // All MMAs issued by this warp must finish before TMEM is released.
+          if (lead) mma_commit(smem_u32(&sh->mma_done));
+          const uint32_t bar = smem_u32(&sh->mma_done);
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(bar, 0) && globaltimer_ns() - t0 < FA_WAIT_TIMEOUT_NS) {
+          }
+        }
+      } else if (lane == 0 && n_max > 0) {
+      bool ok = wait_bar(sh, smem_u32(&sh->q_full), 0, p.status);
+      tc_fence_after();
 
       // ring: K_0, V_0, K_1, V_1, ...  (K_j at position 2j, V_j at 2j+1)
       if (ok) ok = wait_bar(sh, full0, 0, p.status);
@@ -591,6 +689,7 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(bar, 0) && globaltimer_ns() - t0 < FA_WAIT_TIMEOUT_NS) {
         }
+      }
       }
     }
   }
