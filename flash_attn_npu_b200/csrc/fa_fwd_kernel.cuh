@@ -229,7 +229,9 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, __half*) {
 // low mantissa bits of x + 1.5*2^23 and f = x - n in [-0.5, 0.5]; 2^f is a degree-4 polynomial
 // minimising the relative error on that interval (coefficients from csrc/exp2_poly_fit.py, max
 // relative error 2.7e-6 in fp32 Horner form).  2^n is applied by adding n to the exponent
-// field.  x is clamped at -127 so the exponent never underflows past zero (2^-127 ~ 0 here).
+// field.  x is clamped at -126: with n >= -126 and 2^f >= 2^-0.5 (biased exponent >= 126) the
+// exponent field stays >= 0 (at -127 a value 2^f < 1 wrapped into the sign bit and gave a NaN
+// pattern); 2^-126 is ~0 here.
 #ifndef FA_POLY_PAIRS_OF_8
 #define FA_POLY_PAIRS_OF_8 0  // element pairs out of every 8 that use the polynomial
 #endif
@@ -237,8 +239,8 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
   constexpr float c0 = 9.999992847e-01f, c1 = 6.931217909e-01f, c2 = 2.402474433e-01f,
                   c3 = 5.591785908e-02f, c4 = 9.570101276e-03f;
-  x.x = fmaxf(x.x, -127.f);
-  x.y = fmaxf(x.y, -127.f);
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
   const float2 t = fadd2(x, make_float2(kRound, kRound));
   const float2 n = fadd2(t, make_float2(-kRound, -kRound));
   const float2 f = ffma2(n, make_float2(-1.f, -1.f), x);
