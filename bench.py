@@ -363,6 +363,7 @@ def run_ours(args, cfg, world, rank, local):
             torch.backends.cuda.matmul.allow_tf32 = False
             picks = sorted({0, n_slices - 1, n_slices // 3, (2 * n_slices) // 3})
             worst_o = worst_m = worst_l = 0.0
+            lse_ok = True
             for s in picks:
                 b, h = divmod(s, cfg.heads)
                 ro, rl = attention_ref_torch(q_cpu[b, h].to(dev), k_cpu[b, h].to(dev),
@@ -370,11 +371,15 @@ def run_ours(args, cfg, world, rank, local):
                 err = (out_all[s, 0].float() - ro).abs()
                 worst_o = max(worst_o, err.max().item())
                 worst_m = max(worst_m, err.mean().item())
-                worst_l = max(worst_l, (lse_all[s, 0] - rl).abs().max().item())
+                lerr = (lse_all[s, 0] - rl).abs()
+                worst_l = max(worst_l, lerr.max().item())
+                # the parity tests' LSE bar: 1e-4 plus 2e-6 * |lse| (the relative term only
+                # matters for rows with |lse| in the hundreds, e.g. cfg5's outliers, where one
+                # fp32 ulp is already ~3e-5 and the fp32 oracle itself sits that far from fp64)
+                lse_ok = lse_ok and bool((lerr <= 1e-4 + 2e-6 * rl.abs()).all())
             verify = {"slices": picks, "max_abs": worst_o, "mean_abs": worst_m,
-                      "lse_max_abs": worst_l,
-                      "ok": (worst_o <= 2e-2 and worst_m <= 2e-3 and worst_l <= 1e-4
-                             and e2e_equal),
+                      "lse_max_abs": worst_l, "lse_bar": "1e-4 + 2e-6*|lse|",
+                      "ok": (worst_o <= 2e-2 and worst_m <= 2e-3 and lse_ok and e2e_equal),
                       "e2e_bitwise_equal_rank0": e2e_equal,
                       "gathered_with": "nccl p2p" if dist is not None else "local"}
 
