@@ -239,8 +239,14 @@ def run_ours(args, cfg, world, rank, local):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
-    # inputs: drawn on the CPU generator (identical bits on every rank), this rank's slices
+    # inputs: drawn on the CPU generator (identical bits on every rank), this rank's slices.
+    # Every rank draws the full tensors, so with N ranks on one host each takes 1/N of the
+    # cores for it instead of all of them oversubscribing the host.
+    threads = torch.get_num_threads()
+    if world > 1:
+        torch.set_num_threads(max(1, (os.cpu_count() or 1) // world))
     q_cpu, k_cpu, v_cpu = fa_inputs.make_inputs(cfg, "cpu")
+    torch.set_num_threads(threads)
     n_slices = cfg.batch * cfg.heads
     start, stop = sharding.shard_range(n_slices, world, rank)
     n_local = stop - start
