@@ -25,25 +25,20 @@ from . import ops
 
 NBUF = 3                      # device buffers in the ring
 TARGET_CHUNK_BYTES = 96 << 20  # q + k + v bytes per chunk
-MIN_CHUNKS = 8                 # a small call is still cut into this many chunks (slices allowing)
 
 _streams: dict[int, tuple] = {}
 
 
 def plan_chunks(n_slices: int, slice_bytes: int, target_bytes: int = TARGET_CHUNK_BYTES,
-                chunk_slices: int | None = None, tail_split: int = 4,
-                min_chunks: int = MIN_CHUNKS) -> list[tuple[int, int]]:
+                chunk_slices: int | None = None, tail_split: int = 4) -> list[tuple[int, int]]:
     """[start, stop) slice ranges: `chunk_slices` per chunk, or as many as fit `target_bytes`
-    (at least one) but no more than 1/`min_chunks` of the slices, so that a small call still
-    has chunks to overlap (the first chunk's copy-in is the pipeline's un-overlapped head).
-    The remainder goes in the last chunk.  When there is more than one chunk the last one is
-    cut into `tail_split` smaller pieces: the last chunk's kernel and copy-out are the only part
-    of the pipeline no copy-in overlaps."""
+    (at least one), with the remainder in the last chunk.  When there is more than one chunk
+    the last one is cut into `tail_split` smaller pieces: the last chunk's kernel and copy-out
+    are the only part of the pipeline no copy-in overlaps."""
     if n_slices <= 0:
         return []
     if chunk_slices is None:
-        chunk_slices = max(1, min(target_bytes // max(1, slice_bytes),
-                                  -(-n_slices // max(1, min_chunks))))
+        chunk_slices = max(1, target_bytes // max(1, slice_bytes))
     if chunk_slices <= 0:
         raise ValueError("chunk_slices must be positive")
     cs = min(chunk_slices, n_slices)

@@ -20,8 +20,7 @@ def test_plan_chunks_cover_every_slice_once(n, slice_bytes, target, cs):
     sizes = [b - a for a, b in chunks]
     assert all(x > 0 for x in sizes)
     assert all(x >= y for x, y in zip(sizes, sizes[1:]))  # never grows: the tail is split finer
-    full = (min(n, max(1, min(target // slice_bytes, -(-n // host_stream.MIN_CHUNKS))))
-            if cs is None else min(n, cs))
+    full = min(n, max(1, target // slice_bytes)) if cs is None else min(n, cs)
     assert sizes[0] == full
     n_full = -(-n // full)
     if n_full > 1:  # the last uniform chunk became at most 4 pieces
@@ -35,12 +34,7 @@ def test_plan_chunks_edges():
     assert host_stream.plan_chunks(0, 100) == []
     chunks = host_stream.plan_chunks(256, 6 << 20)  # 16-slice chunks, the last one in four
     assert chunks[-5:] == [(224, 240), (240, 244), (244, 248), (248, 252), (252, 256)]
-    assert host_stream.plan_chunks(10, 1, 4, tail_split=1, min_chunks=1) == [(0, 4), (4, 8),
-                                                                               (8, 10)]
-    # a small call is cut into at least MIN_CHUNKS chunks: cfg2 (64 slices of 384 KiB) and one
-    # rank's 32 slices of cfg4 at 8 GPUs
-    assert len(host_stream.plan_chunks(64, 3 << 17)) >= host_stream.MIN_CHUNKS
-    assert host_stream.plan_chunks(32, 6 << 20)[0] == (0, 4)
+    assert host_stream.plan_chunks(10, 1, 4, tail_split=1) == [(0, 4), (4, 8), (8, 10)]
     with pytest.raises(ValueError):
         host_stream.plan_chunks(4, 100, chunk_slices=0)
 
