@@ -323,8 +323,10 @@ def run_ours(args, cfg, world, rank, local):
         vd_l.copy_(v_h, non_blocking=True)
         stream.wait_stream(back)
 
-    # With N ranks on one host all of them copy at once (barrier first, max over ranks), as
-    # in the timed end-to-end steps, so the floor includes their contention for the host.
+    # With N ranks on one host all of them copy at once (barrier first), as in the timed
+    # end-to-end steps, so the floor includes their contention for the host.  Each round's
+    # time is the max over ranks (the round in which all of them copied together); the floor
+    # is the best such round.
     link_ms = float("inf")
     for _ in range(4):
         barrier()
@@ -335,11 +337,12 @@ def run_ours(args, cfg, world, rank, local):
         link_only()
         l1.record(stream)
         torch.cuda.synchronize(dev)
-        link_ms = min(link_ms, l0.elapsed_time(l1))
-    if dist is not None:
-        t = torch.tensor([link_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        link_ms = t.item()
+        round_ms = l0.elapsed_time(l1)
+        if dist is not None:
+            t = torch.tensor([round_ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            round_ms = t.item()
+        link_ms = min(link_ms, round_ms)
     del qd_l, kd_l, vd_l, od_l, ld_l
 
     e2e_step()

@@ -25,6 +25,7 @@ from pathlib import Path
 import torch
 
 from flash_attn_npu_b200 import host_stream as _host_stream
+from flash_attn_npu_b200.ops import check_device_status  # noqa: F401  (device failure check)
 from flash_attn_npu_b200 import ops as _ops
 from flash_attn_npu_b200 import tiling as _tiling
 
@@ -190,13 +191,11 @@ def profile_once(z, h, n_ctx, head_dim, causal, q, k, v, sm_scale):
     out = attention(q, k, v, causal, sm_scale)
     torch.cuda.synchronize()
     runtime = _describe_runtime(z, h, n_ctx, head_dim, causal, dtype=q.dtype)
-    print("CUDA implementation: sm_100a warp-specialised tcgen05 kernel")
-    print(f"Selected tiling config: {runtime['selected_config']} (source={runtime['tiling_source']})")
-    print(
-        "Launch summary: "
-        f"stage={runtime['stage']}, total_tiles={runtime['total_tiles']}, "
-        f"launched_programs={runtime['launched_programs']}"
-    )
+    cfg = runtime["selected_config"]
+    print(f"[{PROFILE_OP_NAME}] tile {cfg['BLOCK_M']}x{cfg['BLOCK_N']} from "
+          f"{runtime['tiling_source']}, ring depth {runtime['pipeline']['NUM_STAGES']}; "
+          f"{runtime['total_tiles']} query tiles on {runtime['launched_programs']} CTAs "
+          f"({'causal' if causal else 'full'} mask)")
     return out
 
 
@@ -223,7 +222,7 @@ def profiling(z, h, n_ctx, head_dim, causal, *args, **kwargs):
     Argument forms match the reference (:1218-1247).  The counters replace the reference's
     torch_npu AiC metric passes (:1262-1289): `flash_attn_npu_b200.ncu_profile` runs this
     module's one-launch `tune` command under `ncu` (metric groups Timing, SpeedOfLight, Memory,
-    Pipes, Issue; only Timing for inputs over 2 GiB).  FA_PROFILE_NCU=0 skips that step; without
+    Pipes, Issue; for inputs over 2 GiB only the launch duration, a single-pass metric).  FA_PROFILE_NCU=0 skips that step; without
     ncu on PATH the summary records why the counters are missing.
     """
     sm_scale_kw = kwargs.pop("sm_scale", None)
@@ -284,9 +283,7 @@ def profiling(z, h, n_ctx, head_dim, causal, *args, **kwargs):
 def _ncu_counters(z, h, n_ctx, head_dim, causal, q, sm_scale):
     """ncu metric groups for one launch of this configuration (in a child process)."""
     from flash_attn_npu_b200 import ncu_profile as _ncu
-    in_bytes = 3 * q.numel() * q.element_size()
-    groups = (_ncu.METRIC_GROUPS if in_bytes <= _ncu.MAX_MULTIPASS_BYTES
-              else {g: _ncu.METRIC_GROUPS[g] for g in _ncu.SINGLE_PASS_GROUPS})
+    groups = _ncu.groups_for_input_bytes(3 * q.numel() * q.element_size())
     argv = [sys.executable, str(Path(__file__).resolve()), "tune", "--z", str(z), "--h", str(h),
             "--n-ctx", str(n_ctx), "--head-dim", str(head_dim),
             "--dtype", str(q.dtype).replace("torch.", ""), "--sm-scale", repr(float(sm_scale))]

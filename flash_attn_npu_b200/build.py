@@ -25,6 +25,17 @@ BUILD_DIR = REPO_DIR / "_build" / "fa_sm100"
 LIB_NAME = "libfa_sm100.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
+# Test builds of the same sources.  "shortwait": every pipeline wait gives up as soon as it
+# is not satisfied at once (FA_WAIT_TIMEOUT_NS = 0), while the teardown drains keep their long
+# limit -- the library the bounded-wait test launches to see the timeout status come back.
+VARIANTS = {
+    "shortwait": ["-DFA_WAIT_TIMEOUT_NS=0ull"],
+}
+
+
+def variant_path(variant: str) -> Path:
+    return PKG_DIR / f"libfa_sm100_{variant}.so"
+
 SOURCES = [
     "fa_fwd_api.cu",
     "fa_fwd_fp32.cu",
@@ -65,18 +76,19 @@ def _inputs_digest(extra_flags: list[str]) -> str:
     return h.hexdigest()
 
 
-def _stamp_path() -> Path:
-    return PKG_DIR / (LIB_NAME + ".sha256")
+def _stamp_path(lib_path: Path = LIB_PATH) -> Path:
+    return lib_path.with_name(lib_path.name + ".sha256")
 
 
-def is_up_to_date(extra_flags: list[str] | None = None) -> bool:
-    stamp = _stamp_path()
-    return LIB_PATH.exists() and stamp.exists() and stamp.read_text().strip() == _inputs_digest(
+def is_up_to_date(extra_flags: list[str] | None = None, lib_path: Path = LIB_PATH) -> bool:
+    stamp = _stamp_path(lib_path)
+    return lib_path.exists() and stamp.exists() and stamp.read_text().strip() == _inputs_digest(
         extra_flags or [])
 
 
-def _compile_one(nvcc: str, src: str, extra: list[str], verbose: bool) -> Path:
-    obj = BUILD_DIR / (Path(src).stem + ".o")
+def _compile_one(nvcc: str, src: str, extra: list[str], verbose: bool,
+                 build_dir: Path = BUILD_DIR) -> Path:
+    obj = build_dir / (Path(src).stem + ".o")
     cmd = [nvcc, *ARCH_FLAGS, *COMMON_FLAGS, *extra, "-I", str(INCLUDE), "-c", str(CSRC / src),
            "-o", str(obj)]
     if verbose:
@@ -89,32 +101,41 @@ def _compile_one(nvcc: str, src: str, extra: list[str], verbose: bool) -> Path:
     return obj
 
 
-def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None) -> Path:
-    """Compile every CUDA source for sm_100a and link `libfa_sm100.so` next to this file."""
+def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None,
+          variant: str | None = None) -> Path:
+    """Compile every CUDA source for sm_100a and link `libfa_sm100.so` next to this file
+    (or, with `variant`, the test library `libfa_sm100_<variant>.so`)."""
     extra = list(extra_flags or [])
-    if not force and is_up_to_date(extra):
-        return LIB_PATH
+    lib_path, build_dir = LIB_PATH, BUILD_DIR
+    if variant is not None:
+        extra = VARIANTS[variant] + extra
+        lib_path = variant_path(variant)
+        build_dir = BUILD_DIR.with_name(f"fa_sm100_{variant}")
+    if not force and is_up_to_date(extra, lib_path):
+        return lib_path
     nvcc = nvcc_path()
-    BUILD_DIR.mkdir(parents=True, exist_ok=True)
+    build_dir.mkdir(parents=True, exist_ok=True)
     workers = min(len(SOURCES), max(1, os.cpu_count() or 1))
     with cf.ThreadPoolExecutor(max_workers=workers) as ex:
-        objs = list(ex.map(lambda s: _compile_one(nvcc, s, extra, verbose), SOURCES))
-    tmp = LIB_PATH.with_suffix(".so.tmp")
+        objs = list(ex.map(lambda s: _compile_one(nvcc, s, extra, verbose, build_dir), SOURCES))
+    tmp = lib_path.with_suffix(".so.tmp")
     cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *[str(o) for o in objs]]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
-    os.replace(tmp, LIB_PATH)
-    _stamp_path().write_text(_inputs_digest(extra) + "\n")
-    return LIB_PATH
+    os.replace(tmp, lib_path)
+    _stamp_path(lib_path).write_text(_inputs_digest(extra) + "\n")
+    return lib_path
 
 
 def main(argv: list[str] | None = None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true", help="print ptxas register/spill report")
+    ap.add_argument("--variant", choices=sorted(VARIANTS), default=None,
+                    help="build a test variant of the library instead of the product")
     args = ap.parse_args(argv)
-    path = build(force=args.force, verbose=args.verbose)
+    path = build(force=args.force, verbose=args.verbose, variant=args.variant)
     print(path)
     return 0
 

@@ -33,7 +33,8 @@
 //
 // Every wait is bounded (FA_WAIT_TIMEOUT_NS); a wait that gives up records
 // FA_ERR_DEVICE_TIMEOUT in *status, raises a CTA-wide abort flag and all roles drain to the
-// teardown, which waits for in-flight copies and MMAs before TMEM is freed.
+// teardown, which waits for in-flight copies and MMAs (bounded separately, FA_DRAIN_TIMEOUT_NS)
+// before TMEM is freed.
 #pragma once
 
 #include <cuda.h>
@@ -46,6 +47,12 @@
 
 #ifndef FA_WAIT_TIMEOUT_NS
 #define FA_WAIT_TIMEOUT_NS 2000000000ull
+#endif
+// Limit of the teardown drains: a role that stops early still waits this long for the TMA
+// loads and MMAs it has issued (they always complete; the limit only bounds the spin).  It is
+// separate from FA_WAIT_TIMEOUT_NS so that a build with a short pipeline limit still drains.
+#ifndef FA_DRAIN_TIMEOUT_NS
+#define FA_DRAIN_TIMEOUT_NS 4000000000ull
 #endif
 
 namespace fa {
@@ -208,6 +215,15 @@ __device__ __forceinline__ bool wait_bar(Shared* sh, uint32_t bar, uint32_t pari
       if (status) atomicCAS(status, 0, kStatusTimeout);
       return false;
     }
+  }
+}
+
+// Drain wait: spins on the phase until it completes or FA_DRAIN_TIMEOUT_NS passes, ignoring
+// the abort flag (it waits for the role's own copies or MMAs, which complete regardless).
+__device__ __forceinline__ void drain_bar(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity) && globaltimer_ns() - t0 < FA_DRAIN_TIMEOUT_NS) {
   }
 }
 
@@ -470,16 +486,14 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
         }
       }
       if (!ok) {
-        // Drain: every load issued must land before the CTA's shared memory goes away.
-        if (q_issued) wait_bar(sh, smem_u32(&sh->q_full), 0, nullptr);
+        // Drain: every load issued must land before the CTA's shared memory goes away.  A
+        // load older than the last `stages` has landed already (its slot was refilled only
+        // after the MMA thread had waited for it).
+        if (q_issued) drain_bar(smem_u32(&sh->q_full), 0);
         const int outstanding = min(issued, stages);
         for (int t = 0; t < outstanding; ++t) {
           const int idx = issued - 1 - t;
-          const uint32_t bar = smem_u32(&sh->full[idx % stages]);
-          const uint32_t par = static_cast<uint32_t>((idx / stages) & 1);
-          const uint64_t t0 = globaltimer_ns();
-          while (!mbar_try_wait(bar, par) && globaltimer_ns() - t0 < FA_WAIT_TIMEOUT_NS) {
-          }
+          drain_bar(smem_u32(&sh->full[idx % stages]), static_cast<uint32_t>((idx / stages) & 1));
         }
       }
     }
@@ -622,10 +636,7 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
           if (ti == 0) take_turn();  // tile 1's last hand-off
           // All MMAs issued by this warp must finish before TMEM is released.
           if (lead) mma_commit(smem_u32(&sh->mma_done));
-          const uint32_t bar = smem_u32(&sh->mma_done);
-          const uint64_t t0 = globaltimer_ns();
-          while (!mbar_try_wait(bar, 0) && globaltimer_ns() - t0 < FA_WAIT_TIMEOUT_NS) {
-          }
+          drain_bar(smem_u32(&sh->mma_done), 0);
         }
       } else if (lane == 0 && n_max > 0) {
       bool ok = wait_bar(sh, smem_u32(&sh->q_full), 0, p.status);
@@ -686,12 +697,7 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
       }
       // All MMAs issued by this thread must finish before TMEM is released.
       mma_commit(smem_u32(&sh->mma_done));
-      {
-        const uint32_t bar = smem_u32(&sh->mma_done);
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(bar, 0) && globaltimer_ns() - t0 < FA_WAIT_TIMEOUT_NS) {
-        }
-      }
+      drain_bar(smem_u32(&sh->mma_done), 0);
       }
     }
   }

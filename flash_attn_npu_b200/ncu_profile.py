@@ -9,8 +9,10 @@ the module's one-launch command (`flash_attention_forward.py tune ...`) under
 
 and the raw page is parsed into the same {group: {metric: value}} shape.  The child command is
 first run once without ncu and must exit 0 (a kernel that faults is never profiled).  Workloads
-whose inputs exceed `MAX_MULTIPASS_BYTES` get only the single-pass timing group: every other
-group needs several replay passes, each saving and restoring device memory.
+whose inputs exceed `MAX_MULTIPASS_BYTES` get `LARGE_INPUT_GROUPS` only -- the launch duration
+`gpu__time_duration.sum`, which ncu collects in one pass.  Every other metric (the clock rate
+included) needs replay passes that save and restore the program's device memory, so those stay
+on inputs below the cap.
 """
 from __future__ import annotations
 
@@ -37,8 +39,14 @@ METRIC_GROUPS: dict[str, list[str]] = {
               "smsp__average_warps_issue_stalled_long_scoreboard_per_issue_active.ratio",
               "launch__registers_per_thread", "launch__grid_size"],
 }
-SINGLE_PASS_GROUPS = ("Timing",)
+# Above the cap only the launch duration is collected (one pass, nothing saved or restored).
+LARGE_INPUT_GROUPS: dict[str, list[str]] = {"Timing": ["gpu__time_duration.sum"]}
 MAX_MULTIPASS_BYTES = 2 << 30
+
+
+def groups_for_input_bytes(in_bytes: int) -> dict[str, list[str]]:
+    """Metric groups one capture may collect for a workload whose q, k, v take `in_bytes`."""
+    return METRIC_GROUPS if in_bytes <= MAX_MULTIPASS_BYTES else LARGE_INPUT_GROUPS
 
 
 def ncu_path() -> str | None:

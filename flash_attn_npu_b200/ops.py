@@ -9,11 +9,14 @@ the B200 kernel keeps the accumulator in TMEM and always uses the stable online 
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _native
 
 HEAD_DIMS = (16, 32, 64, 128, 256)
+_CHECK_EVERY_CALL = os.environ.get("FA_CHECK_STATUS", "0") == "1"
 
 _DTYPE_CODES = {
     torch.float16: _native.FA_DTYPE_FP16,
@@ -63,6 +66,44 @@ def validate_layout(q, k, v) -> None:
     dtype_code(q.dtype)
 
 
+# Device-side failures (a pipeline wait inside the kernel that gave up) are written to an int32
+# status word.  A launch that is not handed one by its caller uses this per-device word, so a
+# failure is never silent: `check_device_status()` reads it (synchronizing the device), and with
+# FA_CHECK_STATUS=1 in the environment every launch is checked right away.  Until a check,
+# `out` and `lse` of a launch that failed on the device are undefined.
+_STATUS_WORDS: dict[int, torch.Tensor] = {}
+
+
+def _device_index(device) -> int:
+    device = torch.device(device)
+    return device.index if device.index is not None else torch.cuda.current_device()
+
+
+def device_status_word(device) -> torch.Tensor:
+    """The per-device int32 status word used by launches that are given none (0 = no failure)."""
+    idx = _device_index(device)
+    word = _STATUS_WORDS.get(idx)
+    if word is None:
+        word = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _STATUS_WORDS[idx] = word
+    return word
+
+
+def check_device_status(device=None) -> None:
+    """Raise RuntimeError if a launch on `device` (default: every device used so far) reported
+    a device-side failure since the last check; the word is then reset.  Synchronizes."""
+    indices = [_device_index(device)] if device is not None else list(_STATUS_WORDS)
+    for idx in indices:
+        word = _STATUS_WORDS.get(idx)
+        if word is None:
+            continue
+        code = int(word.item())
+        if code != 0:
+            word.zero_()
+            raise RuntimeError(f"fa_fwd_sm100 device error {code} on cuda:{idx}: "
+                               f"{_native.status_string(code)}")
+
+
 def _tma_ok(t: torch.Tensor) -> bool:
     """True if `t` can be described by a TMA tensor map as-is (16-byte rule, unit inner stride)."""
     if t.stride(-1) != 1:
@@ -89,7 +130,8 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_
     `block_m/block_n/num_stages/persistent_ctas` = 0 picks the library default.  `out` and
     `lse` may be preallocated (same shape/dtype rules as the freshly allocated ones).
     `status`, if given, is a device int32 tensor of one element that must be zero; a pipeline
-    timeout inside the kernel writes a negative code there.  float32 inputs run in fp32 on the
+    timeout inside the kernel writes a negative code there.  Without one the launch uses the
+    per-device word that `check_device_status()` reads.  float32 inputs run in fp32 on the
     CUDA cores unless `fp32_tf32` selects the (faster, TF32-rounded) tensor-core kernel.
     A float8_e5m2 `v` with float16/bfloat16 `q`, `k` runs the fp8-V kernel (P rounded to e5m2,
     P.V on the fp8 tensor cores); `out` has q's dtype.
@@ -116,6 +158,12 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_
         return out, lse
     if status is not None and (status.dtype != torch.int32 or status.device != q.device):
         raise ValueError("status must be an int32 tensor on the same device")
+    own_status = status is None
+    if own_status and (_device_index(q.device) in _STATUS_WORDS
+                       or not torch.cuda.is_current_stream_capturing()):
+        # (a first launch inside a CUDA-graph capture gets no word: allocating it there would
+        # place it in the graph's private memory pool)
+        status = device_status_word(q.device)
 
     args = _native.make_args(
         q_ptr=qv.data_ptr(), k_ptr=kv.data_ptr(), v_ptr=vv.data_ptr(), o_ptr=out.data_ptr(),
@@ -137,6 +185,8 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_
                             _native.FA_ERR_MISALIGNED):
                 raise ValueError(str(exc)) from None
             raise
+    if own_status and status is not None and _CHECK_EVERY_CALL:
+        check_device_status(q.device)
     return out, lse
 
 

@@ -315,7 +315,7 @@ def test_module_api_on_gpu(cuda_device):
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("case", fa_inputs.EVALUATOR_CORRECTNESS_CASES[:17],
+@pytest.mark.parametrize("case", fa_inputs.EVALUATOR_CORRECTNESS_CASES,
                          ids=lambda c: "x".join(str(int(x)) for x in c))
 def test_reference_evaluator_correctness_cases(case, dtype, cuda_device):
     """The reference evaluator's shapes, inputs and pass rule (allclose atol=rtol=1e-2)."""
@@ -326,3 +326,28 @@ def test_reference_evaluator_correctness_cases(case, dtype, cuda_device):
     ref = attention_ref_torch(q, k, v, causal, 0.5)[0].to(dtype)
     torch.cuda.synchronize()
     assert torch.allclose(ref, out, atol=1e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("idx", range(len(fa_inputs.EVALUATOR_PERFORMANCE_CASES)),
+                         ids=lambda i: "x".join(str(int(x))
+                                                for x in fa_inputs.EVALUATOR_PERFORMANCE_CASES[i]))
+def test_reference_evaluator_performance_shapes_at_preset_tiles(idx, dtype, cuda_device):
+    """The evaluator's six performance shapes at full size, through the module API with the
+    tuned preset each one selects, and with the evaluator's own seeds (seed + 18 + idx) and
+    input recipe.  The evaluator checks every performance case before timing it; here sampled
+    (b, h) slices are held to the parity bar (and to the evaluator's allclose rule)."""
+    import flash_attention_forward as fam
+    z, h, n, d, causal = fa_inputs.EVALUATOR_PERFORMANCE_CASES[idx]
+    assert fam.get_tiling_source(z, h, n, d, causal) == "preset"
+    seed = len(fa_inputs.EVALUATOR_CORRECTNESS_CASES) + idx
+    q, k, v = fa_inputs.evaluator_inputs("cuda", dtype, z, h, n, d, seed)
+    out, lse = fam.attention(q, k, v, causal, 0.5, return_lse=True)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all() and torch.isfinite(lse).all()
+    for b, hh in [(0, 0), (z // 3, h - 1), ((2 * z) // 3, h // 2), (z - 1, 1)]:
+        ro, rl = attention_ref_torch(q[b, hh], k[b, hh], v[b, hh], causal, 0.5)
+        _check(out[b, hh], lse[b, hh], ro, rl)
+        assert torch.allclose(ro.to(dtype), out[b, hh], atol=1e-2, rtol=1e-2)
+    del q, k, v, out, lse
+    torch.cuda.empty_cache()

@@ -115,9 +115,14 @@ def test_tuner_candidate_generation_matches_kernel_family():
     assert all(set(c) == {"BLOCK_M", "BLOCK_N", "NUM_STAGES", "PERSISTENT_CTAS"} for c in cands)
     short = tuner._generate_tiling_candidates((4, 4, 64, 64, True), "bfloat16")
     assert {c["BLOCK_M"] for c in short} == {128}
-    assert tuner._parse_shape_arg("128,8,1024,128,true") == (128, 8, 1024, 128, True)
+    key = tuner.ShapeKey.from_cli("128,8,1024,128,true")
+    assert key.as_tuple() == (128, 8, 1024, 128, True)
+    assert key.key() == "128:8:1024:128:1" and tuner.ShapeKey.from_key(key.key()) == key
+    assert tuner.ShapeKey.from_record(key.record()) == key
     with pytest.raises(ValueError):
-        tuner._parse_shape_arg("1,2,3")
+        tuner.ShapeKey.from_cli("1,2,3")
+    with pytest.raises(ValueError):
+        tuner.ShapeKey.from_cli("1,2,3,4,maybe")
 
 
 def test_tuner_json_merge(tmp_path):
@@ -129,9 +134,16 @@ def test_tuner_json_merge(tmp_path):
            "tuned_configs": {"2:2:128:64:1": {"BLOCK_M": 256, "BLOCK_N": 128, "NUM_STAGES": 4,
                                               "PERSISTENT_CTAS": 0}},
            "results": [{"Z": 2, "H": 2, "N_CTX": 128, "HEAD_DIM": 64, "causal": True, "x": 2}]}
-    merged = tuner._merge_with_existing_output(out, new)
+    merged = tuner.merge_into_existing(out, new)
     assert set(merged["tuned_configs"]) == {"1:1:64:64:0", "2:2:128:64:1"}
     assert [r["x"] for r in merged["results"]] == [1, 2]
+    # a re-tuned shape replaces its row in place
+    again = {"tuned_configs": {"1:1:64:64:0": {"BLOCK_M": 256, "BLOCK_N": 128}},
+             "results": [{"Z": 1, "H": 1, "N_CTX": 64, "HEAD_DIM": 64, "causal": False, "x": 3}]}
+    merged2 = tuner.merge_tuned_payloads(merged, again)
+    assert [r["x"] for r in merged2["results"]] == [3, 2]
+    assert merged2["tuned_configs"]["1:1:64:64:0"]["BLOCK_M"] == 256
+    assert tuner.merge_into_existing(tmp_path / "absent.json", new) is new
 
 
 def test_presets_block_rewrite_roundtrip(tmp_path):
@@ -142,7 +154,7 @@ def test_presets_block_rewrite_roundtrip(tmp_path):
         "16:16:8192:128:0": {"BLOCK_M": 256, "BLOCK_N": 128, "NUM_STAGES": 4,
                              "PERSISTENT_CTAS": 0},
         "128:8:1024:128:1": {"BLOCK_M": 128, "BLOCK_N": 64}}}))
-    tuner.apply_tuned_presets(mod_path, tuned)
+    tuner.write_presets(mod_path, tuned)
     spec = importlib.util.spec_from_file_location("fa_rewritten", mod_path)
     m = importlib.util.module_from_spec(spec)
     sys.path.insert(0, str(REPO))
@@ -152,7 +164,7 @@ def test_presets_block_rewrite_roundtrip(tmp_path):
     assert m.get_tiling_source(128, 8, 1024, 128, True) == "preset"
     assert m.get_tile_config(16, 16, 8192, 128, False)["NUM_STAGES"] == 4
     # a second rewrite replaces the block instead of appending
-    tuner.apply_tuned_presets(mod_path, tuned)
+    tuner.write_presets(mod_path, tuned)
     assert mod_path.read_text().count(tuner.PRESET_BEGIN) == 1
 
 
@@ -253,4 +265,7 @@ def test_ncu_raw_csv_parser_and_groups():
     assert g == {"Timing": {"gpu__time_duration.sum": 1234.0},
                  "Memory": {"dram__bytes_read.sum": 5e6}}
     assert ncu_profile.parse_raw_csv("no csv here") == []
-    assert set(ncu_profile.SINGLE_PASS_GROUPS) <= set(ncu_profile.METRIC_GROUPS)
+    # above the size cap a capture asks for the launch duration alone (one pass)
+    big = ncu_profile.groups_for_input_bytes(ncu_profile.MAX_MULTIPASS_BYTES + 1)
+    assert big == {"Timing": ["gpu__time_duration.sum"]}
+    assert ncu_profile.groups_for_input_bytes(1 << 20) == ncu_profile.METRIC_GROUPS

@@ -25,6 +25,7 @@ torch's scaled_dot_product_attention.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import importlib.util
 import json
 import multiprocessing as mp
@@ -61,41 +62,62 @@ DEFAULT_SHAPES = [
 ]
 
 
-# ------------------------------------------------------------------------- small helpers
-def _load_module(module_path: Path, name: str):
-    spec = importlib.util.spec_from_file_location(name, module_path)
+# ------------------------------------------------------------------------- shape keys
+_TRUE_WORDS = frozenset(("1", "true", "t", "yes", "y"))
+_FALSE_WORDS = frozenset(("0", "false", "f", "no", "n"))
+
+
+@dataclasses.dataclass(frozen=True, order=True)
+class ShapeKey:
+    """One tuned shape.  Its text forms are the interface the tuner shares with its users:
+    `Z:H:N_CTX:HEAD_DIM:causal01` keys in `tuned_configs`, the `Z/H/N_CTX/HEAD_DIM/causal`
+    fields of each `results` row, and `Z,H,N_CTX,HEAD_DIM,causal` on the command line."""
+
+    z: int
+    h: int
+    n_ctx: int
+    head_dim: int
+    causal: bool
+
+    @classmethod
+    def from_cli(cls, text: str) -> "ShapeKey":
+        fields = [f.strip() for f in str(text).split(",")]
+        if len(fields) != 5:
+            raise ValueError(f"--shape wants five comma-separated fields "
+                             f"Z,H,N_CTX,HEAD_DIM,causal; got {text!r}")
+        flag = fields[4].lower()
+        if flag not in _TRUE_WORDS | _FALSE_WORDS:
+            raise ValueError(f"causal field of --shape must be a boolean word, got {fields[4]!r}")
+        return cls(*(int(f) for f in fields[:4]), flag in _TRUE_WORDS)
+
+    @classmethod
+    def from_record(cls, rec: dict) -> "ShapeKey":
+        return cls(int(rec["Z"]), int(rec["H"]), int(rec["N_CTX"]), int(rec["HEAD_DIM"]),
+                   bool(rec["causal"]))
+
+    @classmethod
+    def from_key(cls, key: str) -> "ShapeKey":
+        z, h, n_ctx, head_dim, causal = (int(x) for x in key.split(":"))
+        return cls(z, h, n_ctx, head_dim, bool(causal))
+
+    def key(self) -> str:
+        return ":".join(str(x) for x in (*self.as_tuple()[:4], int(self.causal)))
+
+    def record(self) -> dict:
+        return dict(zip(("Z", "H", "N_CTX", "HEAD_DIM", "causal"), self.as_tuple()))
+
+    def as_tuple(self) -> tuple:
+        return (self.z, self.h, self.n_ctx, self.head_dim, self.causal)
+
+
+def load_module_from_path(path: Path, name: str):
+    """Import a Python file by path (the candidate module or the evaluator)."""
+    spec = importlib.util.spec_from_file_location(name, str(path))
+    if spec is None or spec.loader is None:
+        raise ImportError(f"cannot import {path}")
     module = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(module)
     return module
-
-
-def _parse_shape_arg(raw: str):
-    parts = [part.strip() for part in str(raw).split(",")]
-    if len(parts) != 5:
-        raise ValueError("shape must be formatted as 'Z,H,N_CTX,HEAD_DIM,causal'")
-    z, h, n_ctx, head_dim = (int(value) for value in parts[:4])
-    causal_raw = parts[4].lower()
-    if causal_raw in {"1", "true", "t", "yes", "y"}:
-        causal = True
-    elif causal_raw in {"0", "false", "f", "no", "n"}:
-        causal = False
-    else:
-        raise ValueError(f"invalid causal flag: {parts[4]}")
-    return (z, h, n_ctx, head_dim, causal)
-
-
-def _shape_record(shape):
-    z, h, n_ctx, head_dim, causal = shape
-    return {"Z": z, "H": h, "N_CTX": n_ctx, "HEAD_DIM": head_dim, "causal": causal}
-
-
-def _shape_key_string(shape):
-    z, h, n_ctx, head_dim, causal = shape
-    return f"{z}:{h}:{n_ctx}:{head_dim}:{int(causal)}"
-
-
-def _shape_key_from_record(record: dict):
-    return f"{record['Z']}:{record['H']}:{record['N_CTX']}:{record['HEAD_DIM']}:{int(record['causal'])}"
 
 
 def _dtype_from_name(name: str):
@@ -140,7 +162,7 @@ def _worker_main(module_path, shape, dtype_name, sm_scale, seed, iters, tasks, r
     """Child process: time candidates handed over `tasks` until it receives None."""
     try:
         import torch
-        module = _load_module(Path(module_path), "flash_attention_candidate")
+        module = load_module_from_path(Path(module_path), "flash_attention_candidate")
         z, h, n_ctx, head_dim, causal = shape
         dtype = _dtype_from_name(dtype_name)
         torch.manual_seed(seed)
@@ -306,7 +328,7 @@ def tune_case(module, module_path, eval_module, shape, dtype_name, sm_scale, see
     except Exception as exc:  # noqa: BLE001
         max_abs_diff, correctness_error = None, _error_summary(exc)
     result = {
-        **_shape_record(shape),
+        **ShapeKey(*shape).record(),
         "best_config": best,
         "candidate_avg_us": cand_stats["avg_us"],
         "candidate_min_us": cand_stats["min_us"],
@@ -324,67 +346,58 @@ def tune_case(module, module_path, eval_module, shape, dtype_name, sm_scale, see
     return result
 
 
-def _merge_with_existing_output(output_path: Path, payload: dict):
-    if not output_path.exists():
-        return payload
+def merge_tuned_payloads(previous: dict, current: dict) -> dict:
+    """Resume-by-merge: `current` wins shape by shape; `results` keep first-seen order."""
+    rows: dict[ShapeKey, dict] = {}
+    for row in list(previous.get("results", [])) + list(current.get("results", [])):
+        if isinstance(row, dict):
+            rows[ShapeKey.from_record(row)] = row  # dict keeps the first insertion position
+    merged = dict(current)
+    merged["tuned_configs"] = {**previous.get("tuned_configs", {}),
+                               **current.get("tuned_configs", {})}
+    merged["results"] = list(rows.values())
+    return merged
+
+
+def merge_into_existing(output_path: Path, payload: dict) -> dict:
+    """Merge `payload` with the JSON already at `output_path` (unreadable or absent: as is)."""
     try:
-        existing = json.loads(output_path.read_text(encoding="utf-8"))
-    except Exception:
+        previous = json.loads(output_path.read_text(encoding="utf-8"))
+    except (OSError, ValueError):
         return payload
-    merged_configs = dict(existing.get("tuned_configs", {}))
-    merged_configs.update(payload.get("tuned_configs", {}))
-    merged_results, ordered_keys = {}, []
-    for source in (existing.get("results", []), payload.get("results", [])):
-        for item in source:
-            if not isinstance(item, dict):
-                continue
-            key = _shape_key_from_record(item)
-            if key not in ordered_keys:
-                ordered_keys.append(key)
-            merged_results[key] = item
-    merged_payload = dict(payload)
-    merged_payload["tuned_configs"] = merged_configs
-    merged_payload["results"] = [merged_results[key] for key in ordered_keys]
-    return merged_payload
+    return merge_tuned_payloads(previous, payload) if isinstance(previous, dict) else payload
 
 
-def _format_presets_block(tuned_configs: dict):
-    lines = [
-        PRESET_BEGIN,
-        "# Default tiling presets captured from offline tuning.",
-        "# This block is rewritten by `tune_flash_attention_forward.py`.",
-        "# (Z, H, N_CTX, HEAD_DIM, causal): (BLOCK_M, BLOCK_N, NUM_STAGES, PERSISTENT_CTAS)",
-        "DEFAULT_TILING_PRESETS = {",
-    ]
-    sorted_items = sorted(tuned_configs.items(),
-                          key=lambda item: tuple(int(part) for part in item[0].split(":")))
-    for key, config in sorted_items:
-        z, h, n_ctx, head_dim, causal = key.split(":")
-        causal_bool = "True" if int(causal) else "False"
-        lines.append(
-            f"    ({int(z)}, {int(h)}, {int(n_ctx)}, {int(head_dim)}, {causal_bool}): "
-            f"({int(config['BLOCK_M'])}, {int(config['BLOCK_N'])}, "
-            f"{int(config.get('NUM_STAGES', 0))}, {int(config.get('PERSISTENT_CTAS', 0))}),")
-    lines.append("}")
-    lines.append(PRESET_END)
-    return "\n".join(lines)
+_PRESET_HEADER = (
+    "# Default tiling presets captured from offline tuning.",
+    "# This block is rewritten by `tune_flash_attention_forward.py`.",
+    "# (Z, H, N_CTX, HEAD_DIM, causal): (BLOCK_M, BLOCK_N, NUM_STAGES, PERSISTENT_CTAS)",
+)
 
 
-def apply_tuned_presets(candidate_module_path: Path, tuned_json_path: Path):
-    payload = json.loads(tuned_json_path.read_text(encoding="utf-8"))
-    tuned_configs = payload.get("tuned_configs", {})
+def render_presets_block(tuned_configs: dict) -> str:
+    """The text between (and including) the two markers for a `tuned_configs` table."""
+    knobs = ("BLOCK_M", "BLOCK_N", "NUM_STAGES", "PERSISTENT_CTAS")
+    entries = sorted((ShapeKey.from_key(k), cfg) for k, cfg in tuned_configs.items())
+    body = [f"    {shape.as_tuple()!r}: ({', '.join(str(int(cfg.get(n, 0))) for n in knobs)}),"
+            for shape, cfg in entries]
+    return "\n".join([PRESET_BEGIN, *_PRESET_HEADER, "DEFAULT_TILING_PRESETS = {", *body, "}",
+                      PRESET_END])
+
+
+def write_presets(module_path: Path, tuned_json_path: Path) -> None:
+    """Replace the presets block of `module_path` with the table in `tuned_json_path`."""
+    tuned_configs = json.loads(tuned_json_path.read_text(encoding="utf-8")).get(
+        "tuned_configs") or {}
     if not tuned_configs:
-        raise ValueError(f"no tuned_configs found in {tuned_json_path}")
-    source = candidate_module_path.read_text(encoding="utf-8")
-    begin = source.find(PRESET_BEGIN)
-    end = source.find(PRESET_END)
-    if begin < 0 or end < 0 or end < begin:
-        raise RuntimeError(
-            f"cannot locate preset markers in {candidate_module_path}; expected "
-            f"{PRESET_BEGIN!r} and {PRESET_END!r}")
-    end += len(PRESET_END)
-    updated = source[:begin] + _format_presets_block(tuned_configs) + source[end:]
-    candidate_module_path.write_text(updated, encoding="utf-8")
+        raise ValueError(f"{tuned_json_path} holds no tuned_configs")
+    text = module_path.read_text(encoding="utf-8")
+    head, sep, rest = text.partition(PRESET_BEGIN)
+    _, sep_end, tail = rest.partition(PRESET_END)
+    if not sep or not sep_end:
+        raise RuntimeError(f"{module_path} lacks the preset markers {PRESET_BEGIN!r} / "
+                           f"{PRESET_END!r}")
+    module_path.write_text(head + render_presets_block(tuned_configs) + tail, encoding="utf-8")
 
 
 def build_arg_parser():
@@ -425,20 +438,20 @@ def main(argv=None):
     candidate_module_path = Path(args.candidate_module).resolve()
     output_json_path = Path(args.output_json).resolve()
     if args.apply_only:
-        apply_tuned_presets(candidate_module_path, output_json_path)
+        write_presets(candidate_module_path, output_json_path)
         print(f"Applied tuned presets from {output_json_path} to {candidate_module_path}")
         return 0
 
-    candidate_module = _load_module(candidate_module_path, "flash_attention_candidate")
+    candidate_module = load_module_from_path(candidate_module_path, "flash_attention_candidate")
     evaluate_module = None
     if args.evaluate_module:
         shim = HERE / "flash_attn_npu_b200" / "npu_shim"
         if str(shim) not in sys.path:
             sys.path.insert(0, str(shim))
-        evaluate_module = _load_module(Path(args.evaluate_module).resolve(),
+        evaluate_module = load_module_from_path(Path(args.evaluate_module).resolve(),
                                        "flash_attention_evaluate")
     if args.shape:
-        shapes = [_parse_shape_arg(raw) for raw in args.shape]
+        shapes = [ShapeKey.from_cli(raw).as_tuple() for raw in args.shape]
     elif evaluate_module is not None:
         shapes = [tuple(s) for s in evaluate_module.PERFORMANCE_CASES]
     else:
@@ -457,17 +470,13 @@ def main(argv=None):
               f"speedup={result['speedup_vs_baseline']:.3f}", flush=True)
         results.append(result)
 
-    tuned_table = {
-        _shape_key_string((item["Z"], item["H"], item["N_CTX"], item["HEAD_DIM"],
-                           item["causal"])): item["best_config"]
-        for item in results
-    }
+    tuned_table = {ShapeKey.from_record(item).key(): item["best_config"] for item in results}
     import torch
     payload = {
         "meta": {
-            "candidate_module": str(candidate_module_path),
-            "evaluate_module": str(Path(args.evaluate_module).resolve())
-            if args.evaluate_module else None,
+            # file names only: the JSON is committed and must not carry machine paths
+            "candidate_module": candidate_module_path.name,
+            "evaluate_module": Path(args.evaluate_module).name if args.evaluate_module else None,
             "dtype": args.dtype,
             "sm_scale": args.sm_scale,
             "seed": args.seed,
@@ -482,12 +491,12 @@ def main(argv=None):
         "results": results,
     }
     if not args.replace_output:
-        payload = _merge_with_existing_output(output_json_path, payload)
+        payload = merge_into_existing(output_json_path, payload)
     output_json_path.write_text(json.dumps(payload, indent=2, ensure_ascii=True) + "\n",
                                 encoding="utf-8")
     print(f"Tuned config JSON written to: {output_json_path}")
     if not args.skip_apply:
-        apply_tuned_presets(candidate_module_path, output_json_path)
+        write_presets(candidate_module_path, output_json_path)
         print(f"Applied tuned presets to: {candidate_module_path}")
     return 0
 
