@@ -25,11 +25,13 @@ BUILD_DIR = REPO_DIR / "_build" / "fa_sm100"
 LIB_NAME = "libfa_sm100.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-# Test builds of the same sources.  "shortwait": every pipeline wait gives up as soon as it
-# is not satisfied at once (FA_WAIT_TIMEOUT_NS = 0), while the teardown drains keep their long
-# limit -- the library the bounded-wait test launches to see the timeout status come back.
+# Test builds of the same sources.  "shortwait": every pipeline wait gives up as soon as its
+# first non-suspending probe finds the phase incomplete (FA_WAIT_TIMEOUT_NS = 0, no spin
+# polls), while the teardown drains keep their long limit -- the library the bounded-wait test
+# launches to see the timeout status come back.
 VARIANTS = {
-    "shortwait": ["-DFA_WAIT_TIMEOUT_NS=0ull"],
+    "shortwait": ["-DFA_WAIT_TIMEOUT_NS=0ull", "-DFA_WAIT_SPIN_POLLS=0",
+                  "-DFA_WAIT_POLL_NONBLOCKING"],
 }
 
 

@@ -201,16 +201,31 @@ struct Shared {
 };
 static_assert(sizeof(Shared) <= 256, "barrier block");
 
+// Polls a pipeline wait makes between looks at the clock and the abort flag.  The test build
+// of the bounded waits sets FA_WAIT_POLL_NONBLOCKING, FA_WAIT_SPIN_POLLS = 0 and
+// FA_WAIT_TIMEOUT_NS = 0: a wait whose phase is not complete at its first (non-suspending)
+// probe gives up at once.
+#ifndef FA_WAIT_SPIN_POLLS
+#define FA_WAIT_SPIN_POLLS 32
+#endif
+__device__ __forceinline__ bool wait_poll(uint32_t bar, uint32_t parity) {
+#ifdef FA_WAIT_POLL_NONBLOCKING
+  return mbar_test_wait(bar, parity);
+#else
+  return mbar_try_wait(bar, parity);
+#endif
+}
+
 // Bounded mbarrier wait.  Returns false on timeout or if another role already aborted.
 __device__ __forceinline__ bool wait_bar(Shared* sh, uint32_t bar, uint32_t parity, int* status) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (wait_poll(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    for (int i = 0; i < FA_WAIT_SPIN_POLLS; ++i)
+      if (wait_poll(bar, parity)) return true;
     if (sh->abort_flag) return false;
-    if (globaltimer_ns() - t0 > FA_WAIT_TIMEOUT_NS) {
+    if (globaltimer_ns() - t0 >= FA_WAIT_TIMEOUT_NS) {
       sh->abort_flag = 1u;
       if (status) atomicCAS(status, 0, kStatusTimeout);
       return false;
