@@ -31,7 +31,8 @@ from flash_attn_npu_b200 import tiling as _tiling
 
 DEVICE = "cuda"
 RESULT_DIR_NAME = "result_dir"
-# 0 means "one persistent CTA per SM" (the reference default is 20 programs = 20 Ascend cores).
+# 0 means "one persistent CTA per SM" (the reference default is 20 programs = 20 Ascend cores);
+# it sizes the persistent kernel's grid (float16/bfloat16, HEAD_DIM 64/128, 256 x 128 tiles).
 DEFAULT_PERSISTENT_PROGRAMS = 0
 PROFILE_OP_NAME = "fa_fwd_sm100_kernel"
 
@@ -110,20 +111,38 @@ def _resolve_config(z, h, n_ctx, head_dim, causal, dtype, bm=None, bn=None, stag
             cfg = cfg.replace(num_stages=int(stages))
     ctas = _get_persistent_programs()
     if ctas and not cfg.persistent_ctas:
+        if not _tiling.persistent_kernel_serves(head_dim, dtype, cfg):
+            raise ValueError(
+                f"PERSISTENT_PROGRAMS={ctas} needs the persistent kernel (float16/bfloat16, "
+                f"HEAD_DIM 64 or 128, BLOCK_M 256, BLOCK_N 128); this call resolves to "
+                f"{dtype} HEAD_DIM {head_dim} BLOCK_M {cfg.block_m} BLOCK_N {cfg.block_n}, "
+                f"which launches one CTA per tile")
         cfg = cfg.replace(persistent_ctas=ctas)
     return cfg, source
+
+
+def _sm_count():
+    if torch.cuda.is_available():
+        return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return 148  # B200
 
 
 def _describe_runtime(z, h, n_ctx, head_dim, causal, bm=None, bn=None, dtype=torch.bfloat16):
     cfg, tiling_source = _resolve_config(z, h, n_ctx, head_dim, causal, dtype, bm, bn)
     total_tiles = -(-n_ctx // cfg.block_m) * z * h
+    persistent = _tiling.persistent_kernel_serves(head_dim, dtype, cfg)
+    # the persistent kernel's grid is PERSISTENT_CTAS (0: one CTA per SM), each CTA looping
+    # over tiles; every other configuration launches one CTA per tile
+    launched = (min(total_tiles, cfg.persistent_ctas or _sm_count()) if persistent
+                else total_tiles)
     return {
         "selected_config": {"BLOCK_M": cfg.block_m, "BLOCK_N": cfg.block_n},
         "pipeline": {"NUM_STAGES": cfg.num_stages or _tiling.max_stages(head_dim, dtype, cfg),
                      "PERSISTENT_CTAS": cfg.persistent_ctas},
+        "kernel": "persistent" if persistent else "one CTA per tile",
         "tiling_source": tiling_source,
         "total_tiles": total_tiles,
-        "launched_programs": total_tiles,
+        "launched_programs": launched,
         "stage": 3 if causal else 1,
     }
 

@@ -20,6 +20,7 @@ FA_DTYPE_FP32 = 2
 
 FA_FLAG_FP32_TF32 = 1
 FA_FLAG_V_FP8_E5M2 = 2
+FA_FLAG_ONE_CTA_PER_TILE = 4
 
 FA_OK = 0
 FA_ERR_INVALID_ARG = -1

@@ -57,6 +57,21 @@ int device_ok(int dev) {
   return cache[dev] == 1;
 }
 
+// Streaming multiprocessors of a device (cached; 148 on B200).
+int sm_count(int dev) {
+  static int cache[16] = {0};
+  if (dev < 0 || dev >= 16) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = 148;
+    }
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
 // Element type of a tensor map: an FaDtype, or one byte (fp8 V).
 constexpr int kDtypeByte = 100;
 
@@ -83,6 +98,25 @@ int max_stages_for(const fa::KernelInfo& ki) {
   if (!ki.exists) return 0;
   const int s = (kSmemLimit - ki.smem_fixed) / ki.kv_tile_bytes;
   return std::min(s, kMaxStagesAllowed);
+}
+
+// The persistent warp-specialised kernel (fa_fwd_ws.cuh) serves fp16 / bf16 at head_dim 64 and
+// 128 with (block_m, block_n) = (256, 128); every other configuration runs one CTA per tile.
+bool ws_shape(int64_t head_dim, int dtype, int block_m, int block_n) {
+  return (dtype == FA_DTYPE_FP16 || dtype == FA_DTYPE_BF16) && (head_dim == 64 || head_dim == 128) &&
+         block_m == 256 && block_n == 128;
+}
+
+int ws_max_stages(int64_t head_dim) {
+  const int fixed = head_dim == 64 ? fa::ws_smem_fixed<64>() : fa::ws_smem_fixed<128>();
+  const int stage = head_dim == 64 ? fa::ws_stage_bytes<64>() : fa::ws_stage_bytes<128>();
+  return std::min((kSmemLimit - fixed) / stage, kMaxStagesAllowed);
+}
+
+// Ring depth limit of the kernel that serves these knobs (0 if none).
+int stage_limit(int64_t head_dim, int dtype, int block_m, int block_n, bool vf8) {
+  if (!vf8 && ws_shape(head_dim, dtype, block_m, block_n)) return ws_max_stages(head_dim);
+  return max_stages_for(info_for(head_dim, dtype, block_n, block_m / 128, vf8));
 }
 
 // Encode a 4-D tiled map over a [B, H, S, D] tensor with dims listed innermost first.
@@ -132,7 +166,8 @@ int validate(const FaFwdArgs* a) {
   if (!a->q || !a->k || !a->v || !a->o || !a->lse) return FA_ERR_INVALID_ARG;
   if (!std::isfinite(a->sm_scale)) return FA_ERR_INVALID_ARG;
   if (reinterpret_cast<uintptr_t>(a->lse) % 4 != 0) return FA_ERR_MISALIGNED;
-  if (a->flags & ~(FA_FLAG_FP32_TF32 | FA_FLAG_V_FP8_E5M2)) return FA_ERR_INVALID_ARG;
+  if (a->flags & ~(FA_FLAG_FP32_TF32 | FA_FLAG_V_FP8_E5M2 | FA_FLAG_ONE_CTA_PER_TILE))
+    return FA_ERR_INVALID_ARG;
   if (v_fp8(a)) {
     if (a->dtype == FA_DTYPE_FP32) return FA_ERR_UNSUPPORTED_DTYPE;
     if (a->head_dim < 32) return FA_ERR_UNSUPPORTED_HEAD_DIM;
@@ -143,6 +178,12 @@ int validate(const FaFwdArgs* a) {
 // fp32 inputs without FA_FLAG_FP32_TF32 take the CUDA-core kernel.
 bool use_fp32_simt(const FaFwdArgs* a) {
   return a->dtype == FA_DTYPE_FP32 && !(a->flags & FA_FLAG_FP32_TF32);
+}
+
+// True when this call runs on the persistent kernel.
+bool use_ws(const FaFwdArgs* a, const FaTileConfig& t) {
+  return !v_fp8(a) && !(a->flags & FA_FLAG_ONE_CTA_PER_TILE) && a->sm_scale > 0.f &&
+         ws_shape(a->head_dim, a->dtype, t.block_m, t.block_n);
 }
 
 int resolve_tile(const FaFwdArgs* a, FaTileConfig* t) {
@@ -157,11 +198,14 @@ int resolve_tile(const FaFwdArgs* a, FaTileConfig* t) {
   if (t->block_n != 64 && t->block_n != 128) return FA_ERR_UNSUPPORTED_TILE;
   const fa::KernelInfo ki = info_for(a->head_dim, a->dtype, t->block_n, t->block_m / 128, v_fp8(a));
   if (!ki.exists) return FA_ERR_UNSUPPORTED_TILE;
-  const int smax = max_stages_for(ki);
+  const int smax = stage_limit(a->head_dim, a->dtype, t->block_m, t->block_n, v_fp8(a));
   if (smax < 2) return FA_ERR_UNSUPPORTED_TILE;
   if (t->num_stages == 0) t->num_stages = smax;
   if (t->num_stages < 2 || t->num_stages > smax) return FA_ERR_UNSUPPORTED_TILE;
   if (t->persistent_ctas < 0) return FA_ERR_UNSUPPORTED_TILE;
+  // A persistent grid size only means something to the persistent kernel: refuse it elsewhere
+  // rather than accept a setting that would not be applied.
+  if (t->persistent_ctas > 0 && !use_ws(a, *t)) return FA_ERR_UNSUPPORTED_TILE;
   return FA_OK;
 }
 
@@ -206,8 +250,8 @@ int fa_fwd_sm100_supported(int64_t head_dim, int32_t dtype, int32_t block_m, int
   if (!head_dim_ok(head_dim)) return 0;
   if (block_m != 128 && block_m != 256) return 0;
   if (block_n != 64 && block_n != 128) return 0;
-  const fa::KernelInfo ki = info_for(head_dim, dtype, block_n, block_m / 128);
-  const int smax = max_stages_for(ki);
+  if (!info_for(head_dim, dtype, block_n, block_m / 128).exists) return 0;
+  const int smax = stage_limit(head_dim, dtype, block_m, block_n, false);
   if (smax < 2) return 0;
   if (num_stages == 0) return 1;
   return (num_stages >= 2 && num_stages <= smax) ? 1 : 0;
@@ -215,7 +259,9 @@ int fa_fwd_sm100_supported(int64_t head_dim, int32_t dtype, int32_t block_m, int
 
 int fa_fwd_sm100_max_stages(int64_t head_dim, int32_t dtype, int32_t block_m, int32_t block_n) {
   if (!head_dim_ok(head_dim) || (block_m != 128 && block_m != 256)) return 0;
-  const int s = max_stages_for(info_for(head_dim, dtype, block_n, block_m / 128));
+  if (block_n != 64 && block_n != 128) return 0;
+  if (!info_for(head_dim, dtype, block_n, block_m / 128).exists) return 0;
+  const int s = stage_limit(head_dim, dtype, block_m, block_n, false);
   return s >= 2 ? s : 0;
 }
 
@@ -225,7 +271,15 @@ int64_t fa_fwd_sm100_grid_size(const FaFwdArgs* a) {
   FaTileConfig t;
   if (resolve_tile(a, &t) != FA_OK) return -1;
   const int64_t nq = (a->seqlen + t.block_m - 1) / t.block_m;
-  return nq * a->batch * a->heads;
+  const int64_t tiles = nq * a->batch * a->heads;
+  if (!use_ws(a, t)) return tiles;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    dev = -1;
+  }
+  const int64_t ctas = t.persistent_ctas > 0 ? t.persistent_ctas : sm_count(dev);
+  return std::min(tiles, ctas);
 }
 
 int fa_fwd_sm100(const FaFwdArgs* a, void* stream) {
@@ -272,14 +326,33 @@ int fa_fwd_sm100(const FaFwdArgs* a, void* stream) {
   if (rc == FA_OK)
     rc = encode_map(&lp.tmV, a->v, vf8 ? kDtypeByte : a->dtype, B, H, S, D, a->v_stride,
                     ki.v_box_cols, t.block_n, ki.v_swz_bytes, /*atom32=*/a->dtype == FA_DTYPE_FP32);
+  // The persistent kernel stores O in 128 x 32 boxes with a 64-byte swizzle.
+  const bool ws = use_ws(a, t);
   if (rc == FA_OK)
-    rc = encode_map(&lp.tmO, a->o, a->dtype, B, H, S, D, a->o_stride, ki.box_cols, 128,
-                    ki.swz_bytes);
+    rc = ws ? encode_map(&lp.tmO, a->o, a->dtype, B, H, S, D, a->o_stride, 32, 128, 64)
+            : encode_map(&lp.tmO, a->o, a->dtype, B, H, S, D, a->o_stride, ki.box_cols, 128,
+                         ki.swz_bytes);
   if (rc != FA_OK) return rc;
 
   const int64_t nq = (S + t.block_m - 1) / t.block_m;
   lp.grid = nq * B * H;
   if (lp.grid > 0x7fffffffLL) return FA_ERR_INVALID_ARG;
+  lp.ws = ws;
+  if (lp.ws) {
+    fa::WsParams& w = lp.ws_params;
+    w.batch = static_cast<int>(B);
+    w.heads = static_cast<int>(H);
+    w.seqlen = static_cast<int>(S);
+    w.n_qblocks = static_cast<int>(nq);
+    w.total_tiles = static_cast<int>(lp.grid);
+    w.causal = a->causal ? 1 : 0;
+    w.stages = t.num_stages;
+    w.scale_log2 = a->sm_scale * fa::kLog2e;
+    w.lse = a->lse;
+    w.status = a->dev_status;
+    const int64_t ctas = t.persistent_ctas > 0 ? t.persistent_ctas : sm_count(dev);
+    lp.grid = std::min<int64_t>(lp.grid, ctas);
+  }
   lp.params.batch = static_cast<int>(B);
   lp.params.heads = static_cast<int>(H);
   lp.params.seqlen = static_cast<int>(S);

@@ -9,6 +9,8 @@
 //   fp32, D == 16: none (tf32 MN-major V needs 128-byte rows)
 //   fp32, D == 256: none (a 128-row fp32 query tile plus two K/V stages exceeds 227 KiB)
 //   fp8 V (fp16 / bf16 Q, K), D in {32, 64, 128} : (128,2), (128,1); D == 256 : (128,1), (64,1)
+// plus, for fp16 / bf16 at D in {64, 128}, the persistent warp-specialised kernel
+// (fa_fwd_ws.cuh) behind (block_m, block_n) = (256, 128).
 #pragma once
 
 #include "fa_launch.h"
@@ -24,6 +26,10 @@ template <typename T>
 int dispatch_tile(const LaunchPlan& lp) {
   constexpr int D = FA_HEAD_DIM;
   constexpr bool kF32 = Elt<T>::kTf32;
+  if (lp.ws) {
+    if constexpr (!kF32 && (D == 64 || D == 128)) return launch_ws<T, D>(lp);
+    return -5;
+  }
   if (lp.vf8) {
     if constexpr (!kF32 && D >= 32) {
       if (lp.block_n == 128 && lp.qt == 1) return launch_kernel<T, D, 128, 1, true>(lp);

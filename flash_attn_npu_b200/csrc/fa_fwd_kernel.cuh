@@ -208,29 +208,41 @@ static_assert(sizeof(Shared) <= 256, "barrier block");
 #ifndef FA_WAIT_SPIN_POLLS
 #define FA_WAIT_SPIN_POLLS 32
 #endif
+// FA_WAIT_SUSPEND_HINT_NS > 0: each probe may sleep up to that long for the phase.
+#ifndef FA_WAIT_SUSPEND_HINT_NS
+#define FA_WAIT_SUSPEND_HINT_NS 0
+#endif
 __device__ __forceinline__ bool wait_poll(uint32_t bar, uint32_t parity) {
-#ifdef FA_WAIT_POLL_NONBLOCKING
+#if defined(FA_WAIT_POLL_NONBLOCKING)
   return mbar_test_wait(bar, parity);
+#elif FA_WAIT_SUSPEND_HINT_NS > 0
+  return mbar_try_wait_hint(bar, parity, FA_WAIT_SUSPEND_HINT_NS);
 #else
   return mbar_try_wait(bar, parity);
 #endif
 }
 
-// Bounded mbarrier wait.  Returns false on timeout or if another role already aborted.
-__device__ __forceinline__ bool wait_bar(Shared* sh, uint32_t bar, uint32_t parity, int* status) {
+// Bounded mbarrier wait.  Returns false on timeout or if another role already aborted
+// (`abort_flag` is the CTA's shared abort word).
+__device__ __forceinline__ bool wait_bar_flag(volatile uint32_t* abort_flag, uint32_t bar,
+                                              uint32_t parity, int* status) {
   if (wait_poll(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < FA_WAIT_SPIN_POLLS; ++i)
       if (wait_poll(bar, parity)) return true;
-    if (sh->abort_flag) return false;
+    if (*abort_flag) return false;
     if (globaltimer_ns() - t0 >= FA_WAIT_TIMEOUT_NS) {
-      sh->abort_flag = 1u;
+      *abort_flag = 1u;
       if (status) atomicCAS(status, 0, kStatusTimeout);
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool wait_bar(Shared* sh, uint32_t bar, uint32_t parity, int* status) {
+  return wait_bar_flag(&sh->abort_flag, bar, parity, status);
 }
 
 // Drain wait: spins on the phase until it completes or FA_DRAIN_TIMEOUT_NS passes, ignoring
@@ -280,6 +292,27 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   q = ffma2(q, f, make_float2(c1, c1));
   q = ffma2(q, f, make_float2(c0, c0));
   // bits(t) = bits(kRound) + n and bits(kRound) << 23 == 0 (mod 2^32): (bits(t) << 23) == n << 23
+  q.x = __int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23));
+  q.y = __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23));
+  return q;
+}
+
+// Degree-3 variant of the same routine (one FMA pair fewer; max relative error 7.5e-5, from
+// csrc/exp2_poly_fit.py with degree 3).  The persistent kernel routes a minority of its exp2s
+// here: P is rounded to 16 bits (relative step 2^-8 .. 2^-11) and the row sum l mixes these
+// values with ex2.approx ones, which keeps the logsumexp well inside its 1e-4 bar.
+__device__ __forceinline__ float2 exp2_poly2_deg3(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c0 = 9.999280572e-01f, c1 = 6.932609677e-01f, c2 = 2.426111251e-01f,
+                  c3 = 5.517166480e-02f;
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = fadd2(x, make_float2(kRound, kRound));
+  const float2 n = fadd2(t, make_float2(-kRound, -kRound));
+  const float2 f = ffma2(n, make_float2(-1.f, -1.f), x);
+  float2 q = ffma2(make_float2(c3, c3), f, make_float2(c2, c2));
+  q = ffma2(q, f, make_float2(c1, c1));
+  q = ffma2(q, f, make_float2(c0, c0));
   q.x = __int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23));
   q.y = __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23));
   return q;
@@ -500,10 +533,12 @@ __global__ void __launch_bounds__(Geo<T, D, BN, QT, VF8>::NUM_THREADS, 1)
           }
         }
       }
-      if (!ok) {
-        // Drain: every load issued must land before the CTA's shared memory goes away.  A
+      {
+        // Drain, on every path (another role may have stopped after the last load was
+        // issued): every load issued must land before the CTA's shared memory goes away.  A
         // load older than the last `stages` has landed already (its slot was refilled only
-        // after the MMA thread had waited for it).
+        // after the MMA thread had waited for it); in a run without abort these waits return
+        // at once.
         if (q_issued) drain_bar(smem_u32(&sh->q_full), 0);
         const int outstanding = min(issued, stages);
         for (int t = 0; t < outstanding; ++t) {

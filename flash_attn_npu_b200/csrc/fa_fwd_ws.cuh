@@ -1,0 +1,717 @@
+// Persistent, warp-specialised FlashAttention forward for B200 (sm_100a): the kernel behind
+// the 256-row query blocks (two 128-row tiles) of 16-bit inputs at head_dim 64 and 128.
+//
+// What it computes is the reference's `_attn_fwd` (flash_attention_forward.py:1036-1111):
+//   O[b,h,i,:] = sum_j softmax_j(scale * q_i . k_j) v_j   (keys j <= i when causal)
+//   LSE[b,h,i] = log sum_j exp(scale * q_i . k_j)
+// with the reference's persistent driver -- each program loops over tiles
+// `for tile in range(pid, total_tiles, num_programs)` (:1071-1076), grid = PERSISTENT_PROGRAMS
+// (:616-623, :1125-1127) -- and the reference's tile orders (non-causal: the query blocks of
+// one head adjacent; causal: longest query blocks first, :915-922).
+//
+// Roles (16 warps, one CTA per SM):
+//   warps 0-3   softmax, query tile 0   (thread r owns row r = TMEM lane r)
+//   warps 4-7   softmax, query tile 1
+//   warps 8-11  correction: rescales O_i in TMEM when a row's exponent base moves, and writes
+//               the output tile (O / l -> shared memory -> TMA store)
+//   warp 12     TMEM allocator; tcgen05.mma issuer of query tile 0 (lane 0)
+//   warp 13     TMA producer (Q tiles, then the K/V ring)
+//   warp 14     tcgen05.mma issuer of query tile 1 (the two issuers take turns)
+//   warp 15     idle (it completes the fourth warpgroup for the register split)
+//
+// TMEM: S_i (fp32 logits, 128 columns) at 128 i; P_i (16-bit probabilities) over the first 64
+// columns of S_i; O_i (fp32, D columns) at 256 + D i.
+//
+// One KV step j, per tile i, issued by tile i's MMA warp in its turn, once P_i(j) is in TMEM
+// and the correction warps have rescaled O_i:
+//   O_i (+)= P_i V_j ;  S_i = Q_i K_{j+1}^T  (commit: S_i full)
+// The softmax warpgroup of tile i, per step: load S_i, row max, pick the exponent base
+// (it moves only when the row max passes it by more than 8 in log2 units, so O and l rarely
+// need rescaling), hand the per-row rescale factor to the correction warps, exponentiate
+// (ex2.approx, with a fixed minority of element pairs on the FMA pipe), store P_i in four
+// 32-key chunks -- the first three released together, the last one on its own -- and only
+// then add the row sum, which is off the path to the next MMA.
+//
+// Every wait is bounded (FA_WAIT_TIMEOUT_NS); a wait that gives up records
+// FA_ERR_DEVICE_TIMEOUT in the status word and raises the CTA's abort flag, after which every
+// role leaves its loop and drains what it has in flight (FA_DRAIN_TIMEOUT_NS) before TMEM is
+// freed.  The only unbounded synchronisation is the final __syncthreads, which every thread
+// reaches exactly once.
+#pragma once
+
+#include "fa_fwd_kernel.cuh"
+
+namespace fa {
+
+struct WsParams {
+  int batch;
+  int heads;
+  int seqlen;
+  int n_qblocks;    // ceil(seqlen / 256)
+  int total_tiles;  // n_qblocks * batch * heads
+  int causal;
+  int stages;       // K/V ring depth
+  float scale_log2; // > 0 (the host routes other scales to the one-CTA-per-tile kernel)
+  float* lse;
+  int* status;
+};
+
+// Element pairs (of the 16 in each 32-key chunk) that take the FMA-pipe exp2 in chunks 1 and
+// 2; chunk 0 and the last chunk use ex2.approx only.  6 -> 12 of 64 pairs (18.75 %).
+#ifndef FA_WS_EMU_PAIRS
+#define FA_WS_EMU_PAIRS 0
+#endif
+// Release P in two parts (first 96 keys, then the last 32) so the P.V MMAs start before the
+// softmax has finished the row.  0 releases the whole P at once.
+#ifndef FA_WS_SPLIT_P
+#define FA_WS_SPLIT_P 0
+#endif
+
+template <typename T, int D>
+struct WsGeo {
+  static_assert(D == 64 || D == 128, "persistent kernel: head_dim 64 or 128");
+  static constexpr int BN = 128;                  // keys per step
+  static constexpr int BM = 128;                  // rows per query tile
+  static constexpr int ROW_BYTES = D * 2;
+  static constexpr int SWZ = 128;                 // 128-byte swizzle spans
+  static constexpr int BLK_COLS = 64;             // elements per span
+  static constexpr int NBLK = ROW_BYTES / SWZ;    // spans per row (1 or 2)
+  static constexpr int Q_BLK_BYTES = BM * SWZ;    // 16 KiB
+  static constexpr int Q_TILE_BYTES = BM * ROW_BYTES;
+  static constexpr int KV_BLK_BYTES = BN * SWZ;
+  static constexpr int KV_TILE_BYTES = BN * ROW_BYTES;
+  // Output: 128 x 32 boxes (64-byte rows, 64-byte swizzle), double-buffered in shared memory
+  // so one box's TMA store drains while the next one is written.
+  static constexpr int O_BOX_COLS = 32;
+  static constexpr int O_SWZ = 64;
+  static constexpr int STAGE_BYTES = BM * O_SWZ;  // 8 KiB
+  static constexpr int N_OSTAGE = 2;
+  static constexpr int QK_MMAS = NBLK * (SWZ / 32);  // K = 16 elements = 32 bytes per MMA
+  static constexpr int PV_MMAS = BN / 16;
+  static constexpr int PV_SPLIT = FA_WS_SPLIT_P ? 6 : PV_MMAS;  // MMAs on the first 96 keys
+  static constexpr int TMEM_S = 0;
+  static constexpr int TMEM_O = 2 * BN;
+  static constexpr int TMEM_ALLOC = 512;
+  static constexpr int NUM_THREADS = 512;
+  // Register split: launched at 128 per thread (65536 / 512); the two softmax warpgroups
+  // take 184, the correction warpgroup 88, the producer/MMA warpgroup 56:
+  // 256 * 184 + 128 * 88 + 128 * 56 = 65536.
+#ifndef FA_WS_REG_SOFTMAX
+#define FA_WS_REG_SOFTMAX 184
+#define FA_WS_REG_CORR 88
+#define FA_WS_REG_OTHER 56
+#endif
+  static constexpr int REG_SOFTMAX = FA_WS_REG_SOFTMAX;
+  static constexpr int REG_CORR = FA_WS_REG_CORR;
+  static constexpr int REG_OTHER = FA_WS_REG_OTHER;
+  static_assert(256 * REG_SOFTMAX + 128 * REG_CORR + 128 * REG_OTHER <= NUM_THREADS * 128,
+                "register split must fit the launch allocation");
+  static constexpr uint32_t LAYOUT = 2u;  // SWIZZLE_128B
+  static constexpr uint32_t IDESC_S = make_idesc(Elt<T>::kFmt, false, 128, BN);
+  static constexpr uint32_t IDESC_O = make_idesc(Elt<T>::kFmt, true, 128, D);
+};
+
+struct WsShared {
+  uint64_t q_full[2], q_empty[2];
+  uint64_t kv_full[kMaxStages], kv_empty[kMaxStages];
+  uint64_t s_full[2];   // MMA -> softmax: S_i(j) computed
+  uint64_t p_ready[2];  // softmax (first 3/4 of P) + correction (O rescaled) -> MMA
+  uint64_t p_last[2];   // softmax (last 1/4 of P) -> MMA
+  uint64_t stats[2];    // softmax -> correction: acc_scale of step j >= 1 written
+  uint64_t fin[2];      // softmax -> correction: inv_l of the tile written
+  uint64_t fin_free[2]; // correction -> softmax: inv_l read, the next tile may overwrite it
+  uint64_t o_full[2];   // MMA -> correction: last P.V of the tile done
+  uint64_t o_empty[2];  // correction -> MMA: O_i read out, the next tile may overwrite it
+  uint64_t ost_full[2]; // correction warps -> store thread: staging buffer written
+  uint64_t ost_free[2]; // store thread -> correction warps: staging buffer read by TMA
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  volatile uint32_t abort_flag;
+  float acc_scale[2][128];
+  float inv_l[2][128];
+};
+
+template <int D>
+constexpr int ws_smem_bytes(int stages) {
+  using G = WsGeo<__nv_bfloat16, D>;
+  return 1024 + 2 * G::Q_TILE_BYTES + stages * G::KV_TILE_BYTES +
+         G::N_OSTAGE * G::STAGE_BYTES + static_cast<int>(sizeof(WsShared));
+}
+
+// Tile coordinates shared by every role: query block, (batch, head), KV steps per query tile.
+struct WsTile {
+  int qblk, bh, bi, hi, q0;
+  int n[2];
+  int n_max;
+};
+
+__device__ __forceinline__ WsTile ws_tile(const WsParams& p, int t) {
+  WsTile w;
+  const int bh_count = p.batch * p.heads;
+  if (p.causal) {
+    w.qblk = p.n_qblocks - 1 - t / bh_count;
+    w.bh = t % bh_count;
+  } else {
+    w.bh = t / p.n_qblocks;
+    w.qblk = t % p.n_qblocks;
+  }
+  w.bi = w.bh / p.heads;
+  w.hi = w.bh % p.heads;
+  w.q0 = w.qblk * 256;
+  w.n_max = 0;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int row0 = w.q0 + 128 * i;
+    if (row0 >= p.seqlen) {
+      w.n[i] = 0;
+    } else {
+      const int kv_end = p.causal ? min(p.seqlen, row0 + 128) : p.seqlen;
+      w.n[i] = (kv_end + 127) / 128;
+    }
+    w.n_max = max(w.n_max, w.n[i]);
+  }
+  return w;
+}
+
+// Bounded wait of one thread, and the warp-collective form (every lane polls, the warp agrees
+// on the outcome).
+__device__ __forceinline__ bool ws_wait1(WsShared* sh, uint32_t bar, uint32_t parity, int* status) {
+  return wait_bar_flag(&sh->abort_flag, bar, parity, status);
+}
+__device__ __forceinline__ bool ws_wait(WsShared* sh, uint32_t bar, uint32_t parity, int* status) {
+  return __all_sync(0xffffffffu, ws_wait1(sh, bar, parity, status));
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(512, 1)
+    fa_fwd_ws_kernel(const __grid_constant__ CUtensorMap tmQ,
+                     const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV,
+                     const __grid_constant__ CUtensorMap tmO, const WsParams p) {
+  using G = WsGeo<T, D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* q_smem = smem;                                   // 2 query tiles
+  uint8_t* kv_smem = q_smem + 2 * G::Q_TILE_BYTES;          // K/V ring
+  uint8_t* o_stage = kv_smem + p.stages * G::KV_TILE_BYTES;  // output staging
+  WsShared* sh = reinterpret_cast<WsShared*>(o_stage + G::N_OSTAGE * G::STAGE_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int stages = p.stages;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(smem_u32(&sh->kv_full[s]), 1);
+      mbar_init(smem_u32(&sh->kv_empty[s]), 2);  // one commit per MMA-issuing warp
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&sh->q_full[i]), 1);
+      mbar_init(smem_u32(&sh->q_empty[i]), 1);
+      mbar_init(smem_u32(&sh->s_full[i]), 1);
+      mbar_init(smem_u32(&sh->p_ready[i]), 8);  // 4 softmax warps + 4 correction warps
+      mbar_init(smem_u32(&sh->p_last[i]), 4);
+      mbar_init(smem_u32(&sh->stats[i]), 4);
+      mbar_init(smem_u32(&sh->fin[i]), 4);
+      mbar_init(smem_u32(&sh->fin_free[i]), 4);
+      mbar_init(smem_u32(&sh->o_full[i]), 1);
+      mbar_init(smem_u32(&sh->o_empty[i]), 4);
+      mbar_init(smem_u32(&sh->ost_full[i]), 4);
+      mbar_init(smem_u32(&sh->ost_free[i]), 1);
+    }
+    mbar_init(smem_u32(&sh->mma_done), 2);  // one commit per MMA-issuing warp
+    sh->abort_flag = 0u;
+    fence_mbar_init();
+  }
+  if (warp == 13 && lane == 0) {
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+    prefetch_tmap(&tmO);
+  }
+  if (warp == 12) {
+    tmem_alloc(smem_u32(&sh->tmem_base), G::TMEM_ALLOC);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+  const int t_first = static_cast<int>(blockIdx.x);
+  const int t_step = static_cast<int>(gridDim.x);
+
+  if (warp >= 12) {
+    setmaxnreg_dec<G::REG_OTHER>();
+    if (warp == 13) {
+      // ============================================================ TMA producer
+      if (lane == 0) {
+        uint32_t qe_ph[2] = {0u, 0u};
+        int slot = 0;
+        uint32_t ph = 0;
+        int issued = 0;       // K/V loads issued
+        bool q_pending[2] = {false, false};
+        uint32_t q_par[2] = {0u, 0u};  // parity of the last Q load's q_full phase
+        bool ok = true;
+        for (int t = t_first; t < p.total_tiles && ok; t += t_step) {
+          const WsTile w = ws_tile(p, t);
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            if (w.n[i] == 0 || !ok) continue;
+            // the previous tile's last Q_i K^T has completed
+            if (!ws_wait1(sh, smem_u32(&sh->q_empty[i]), qe_ph[i] ^ 1u, p.status)) {
+              ok = false;
+              break;
+            }
+            qe_ph[i] ^= 1u;
+            const uint32_t qb = smem_u32(&sh->q_full[i]);
+            mbar_arrive_expect_tx(qb, G::Q_TILE_BYTES);
+#pragma unroll
+            for (int c = 0; c < G::NBLK; ++c)
+              tma_load_4d(smem_u32(q_smem + i * G::Q_TILE_BYTES + c * G::Q_BLK_BYTES), &tmQ, qb,
+                          c * G::BLK_COLS, w.q0 + 128 * i, w.hi, w.bi);
+            q_par[i] = q_pending[i] ? q_par[i] ^ 1u : 0u;
+            q_pending[i] = true;
+          }
+          for (int j = 0; j < w.n_max && ok; ++j) {
+#pragma unroll
+            for (int kv = 0; kv < 2; ++kv) {
+              if (!ws_wait1(sh, smem_u32(&sh->kv_empty[slot]), ph ^ 1u, p.status)) {
+                ok = false;
+                break;
+              }
+              const uint32_t fb = smem_u32(&sh->kv_full[slot]);
+              uint8_t* dst = kv_smem + slot * G::KV_TILE_BYTES;
+              mbar_arrive_expect_tx(fb, G::KV_TILE_BYTES);
+#pragma unroll
+              for (int c = 0; c < G::NBLK; ++c)
+                tma_load_4d(smem_u32(dst + c * G::KV_BLK_BYTES), kv == 0 ? &tmK : &tmV, fb,
+                            c * G::BLK_COLS, j * G::BN, w.hi, w.bi);
+              ++issued;
+              if (++slot == stages) {
+                slot = 0;
+                ph ^= 1u;
+              }
+            }
+          }
+        }
+        // Drain, on every path (another role may stop after the last load was issued): the
+        // loads this thread issued land before shared memory goes away -- the last Q load of
+        // each tile slot and the last `stages` K/V loads (older ones landed before their slots
+        // were refilled).  Without an abort these phases have completed already.
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          if (q_pending[i]) drain_bar(smem_u32(&sh->q_full[i]), q_par[i]);
+        const int outstanding = min(issued, stages);
+        for (int u = 0; u < outstanding; ++u) {
+          const int idx = issued - 1 - u;
+          drain_bar(smem_u32(&sh->kv_full[idx % stages]),
+                    static_cast<uint32_t>((idx / stages) & 1));
+        }
+      }
+    } else if (warp == 12 || warp == 14) {
+      // ============================================================ MMA issuers
+      // Warp 12 issues query tile 0's MMAs, warp 14 tile 1's, taking turns through two named
+      // barriers: per tile, S_0(0), S_1(0); then per KV step j, tile 0's P V_j (+ Q K_{j+1}^T)
+      // and tile 1's.  The tensor pipe sees one issuer's order, while each warp waits for its
+      // own operands (V_j, K_{j+1}, P_i(j), O_i) during the other warp's MMAs -- a satisfied
+      // mbarrier wait still costs a few hundred cycles, and the pipe holds little more than the
+      // MMA in flight.  Turn passing: barrier kTok0 (tile 0 done -> tile 1 may issue), kTok1
+      // (the reverse); bar.arrive by the passer, bar.sync by the taker.  Both warps walk the
+      // same tiles and steps and make a hand-off on every turn whatever happens (a wait that
+      // gives up only stops the issuing), so neither is left in bar.sync.
+      // Shared-memory descriptors as low words (start address >> 4 | leading offset >> 4 << 16)
+      // plus one high word: stride 1024 B (8 rows of 128 B), version 1, 128-byte swizzle.  The
+      // start-address field never carries (shared memory < 256 KiB), so offsets add to the low
+      // word.  Q and K are K-major (leading offset unused), V is MN-major with its two 64-column
+      // spans KV_BLK_BYTES apart.
+      // A K/V slot's empty barrier counts two arrivals, one commit per issuer per use: each
+      // commit follows every MMA its warp issued on the slot, so the slot is refilled only
+      // after both tiles' MMAs on it have completed.
+      constexpr uint32_t kTok0 = 1, kTok1 = 2;
+      const int ti = warp == 12 ? 0 : 1;
+      constexpr uint32_t kHi = (1024u >> 4) | (1u << 14) | (G::LAYOUT << 29);
+      const uint32_t q_lo = (smem_u32(q_smem + ti * G::Q_TILE_BYTES) >> 4) | (1u << 16);
+      const uint32_t k_lo = (smem_u32(kv_smem) >> 4) | (1u << 16);
+      const uint32_t v_lo = (smem_u32(kv_smem) >> 4) | (static_cast<uint32_t>(G::KV_BLK_BYTES >> 4) << 16);
+      const uint32_t hi = kHi;
+      constexpr uint32_t kSlotStep = G::KV_TILE_BYTES >> 4;
+      const uint32_t full0 = smem_u32(&sh->kv_full[0]);
+      const uint32_t empty0 = smem_u32(&sh->kv_empty[0]);
+      const uint32_t s_bar = smem_u32(&sh->s_full[ti]);
+      const uint32_t pr_bar = smem_u32(&sh->p_ready[ti]);
+      const uint32_t pl_bar = smem_u32(&sh->p_last[ti]);
+      const uint32_t oe_bar = smem_u32(&sh->o_empty[ti]);
+      const uint32_t qe_bar = smem_u32(&sh->q_empty[ti]);
+      const uint32_t dS = tmem + G::TMEM_S + ti * G::BN;
+      const uint32_t dO = tmem + G::TMEM_O + ti * D;
+      const bool lead = lane == 0;
+
+      auto issue_s = [&](int kslot) {
+        const uint32_t b0 = k_lo + static_cast<uint32_t>(kslot) * kSlotStep;
+#pragma unroll
+        for (int c = 0; c < G::NBLK; ++c) {
+#pragma unroll
+          for (int kk = 0; kk < G::SWZ / 32; ++kk)
+            mma_f16_ss_lo(dS, q_lo + ((c * G::Q_BLK_BYTES + kk * 32) >> 4),
+                          b0 + ((c * G::KV_BLK_BYTES + kk * 32) >> 4), hi, G::IDESC_S,
+                          (c | kk) ? 1u : 0u);
+        }
+      };
+      // O (+)= P V for the key groups [k0, k1) of 16 keys
+      auto issue_pv = [&](int vslot, int k0, int k1, uint32_t acc_first) {
+        const uint32_t b0 = v_lo + static_cast<uint32_t>(vslot) * kSlotStep;
+#pragma unroll
+        for (int kk = k0; kk < k1; ++kk)
+          mma_f16_ts_lo(dO, dS + kk * 8, b0 + ((kk * 16 * G::SWZ) >> 4), hi, G::IDESC_O,
+                        kk > 0 ? 1u : acc_first);
+      };
+      auto pass_turn = [&]() {
+        __syncwarp();
+        named_barrier_arrive(ti == 0 ? kTok0 : kTok1, 64);
+      };
+      auto take_turn = [&]() {
+        __syncwarp();
+        named_barrier_sync(ti == 0 ? kTok1 : kTok0, 64);
+      };
+
+      // phase bits of this tile's barriers: q_full (0), p_ready (1), p_last (2), o_empty (3)
+      uint32_t phs = 0;
+      int slot = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      bool first_turn = true;  // tile 0's very first turn is the only one without a take
+      for (int t = t_first; t < p.total_tiles; t += t_step) {
+        const WsTile w = ws_tile(p, t);
+        const int mine = ti == 0 ? w.n[0] : w.n[1];
+        // ---- turn: S(0) = Q K_0^T
+        const int k0slot = slot;
+        if (ok) ok = ws_wait(sh, full0 + 8u * slot, ph, p.status);
+        if (++slot == stages) { slot = 0; ph ^= 1u; }
+        if (ok && mine > 0) {
+          ok = ws_wait(sh, smem_u32(&sh->q_full[ti]), phs & 1u, p.status);
+          phs ^= 1u;
+        }
+        tc_fence_after();
+        if (ti == 1 || !first_turn) take_turn();
+        first_turn = false;
+        if (ok && lead) {
+          if (mine > 0) {
+            issue_s(k0slot);
+            mma_commit(s_bar);
+            if (mine == 1) mma_commit(qe_bar);
+          }
+          mma_commit(empty0 + 8u * k0slot);
+        }
+        pass_turn();
+        for (int j = 0; j < w.n_max; ++j) {
+          // ---- turn: P V_j (+ Q K_{j+1}^T); ring order K_0, V_0, K_1, V_1, ...
+          const bool act = j < mine;
+          const bool s_next = j + 1 < mine;
+          const int vslot = slot;
+          const uint32_t vph = ph;
+          if (++slot == stages) { slot = 0; ph ^= 1u; }
+          const bool k_next = j + 1 < w.n_max;
+          const int kslot = slot;
+          const uint32_t kph = ph;
+          if (k_next && ++slot == stages) { slot = 0; ph ^= 1u; }
+          if (ok && act) ok = ws_wait(sh, full0 + 8u * vslot, vph, p.status);
+          if (ok && s_next) ok = ws_wait(sh, full0 + 8u * kslot, kph, p.status);
+          if (ok && act) {
+            ok = ws_wait(sh, pr_bar, (phs >> 1) & 1u, p.status);
+            phs ^= 2u;
+          }
+          if (ok && act && j == 0) {
+            // the previous tile's output has been read out of O
+            ok = ws_wait(sh, oe_bar, ((phs >> 3) & 1u) ^ 1u, p.status);
+            phs ^= 8u;
+          }
+          if constexpr (G::PV_SPLIT < G::PV_MMAS) {
+            if (ok && act) {
+              ok = ws_wait(sh, pl_bar, (phs >> 2) & 1u, p.status);
+              phs ^= 4u;
+            }
+          }
+          tc_fence_after();
+          take_turn();
+          if (ok && lead) {
+            if (act) {
+              issue_pv(vslot, 0, G::PV_MMAS, j > 0 ? 1u : 0u);
+              if (s_next) {
+                issue_s(kslot);
+                mma_commit(s_bar);
+                if (j + 2 == mine) mma_commit(qe_bar);
+              } else {
+                mma_commit(smem_u32(&sh->o_full[ti]));
+              }
+            }
+            mma_commit(empty0 + 8u * vslot);
+            if (k_next) mma_commit(empty0 + 8u * kslot);
+          }
+          pass_turn();
+        }
+      }
+      if (ti == 0) take_turn();  // tile 1's last hand-off
+      // every MMA this warp issued completes before TMEM is released
+      if (lead) mma_commit(smem_u32(&sh->mma_done));
+      __syncwarp();
+      drain_bar(smem_u32(&sh->mma_done), 0);
+    }
+  } else if (warp >= 8) {
+    setmaxnreg_dec<G::REG_CORR>();
+    // ================================================================ correction
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const bool store_thread = warp == 8 && lane == 0;
+    // phase bits: stats (bit i), o_full (2 + i), fin (4 + i), staging free (6 + b, waited
+    // producer-style), staging written (8 + b, store thread); "step 0 already signalled" (10 + i)
+    uint32_t phs = 0;
+    int ostage = 0;
+    bool ok = true;
+    bool stores_issued = false;
+
+    auto arrive_p_ready = [&](int i) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sh->p_ready[i]));
+    };
+
+    for (int t = t_first; t < p.total_tiles && ok; t += t_step) {
+      const WsTile w = ws_tile(p, t);
+      for (int j = 0; j < w.n_max && ok; ++j) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          if (j >= w.n[i] || !ok) continue;
+          if (j == 0) {
+            // step 0 starts O_i from zero: nothing to rescale
+            if (!((phs >> (10 + i)) & 1u)) arrive_p_ready(i);
+            phs &= ~(1u << (10 + i));
+            continue;
+          }
+          ok = ws_wait(sh, smem_u32(&sh->stats[i]), (phs >> i) & 1u, p.status);
+          if (!ok) break;
+          phs ^= 1u << i;
+          const float a = sh->acc_scale[i][r];
+          if (__any_sync(0xffffffffu, a < 1.f)) {
+            // O_i holds P V summed over steps < j (S_i(j) is complete, and the MMAs of one
+            // thread complete in order); rescale this warp's 32 rows
+            tc_fence_after();
+            const uint32_t tO = tmem + lane_off + G::TMEM_O + i * D;
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld32(tO + c * 32, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int u = 0; u < 32; u += 2) {
+                const float2 v = fmul2(make_float2(__uint_as_float(o[u]), __uint_as_float(o[u + 1])),
+                                       make_float2(a, a));
+                o[u] = __float_as_uint(v.x);
+                o[u + 1] = __float_as_uint(v.y);
+              }
+              tmem_st32(tO + c * 32, o);
+            }
+            tmem_wait_st();
+          }
+          arrive_p_ready(i);
+        }
+      }
+      if (!ok) break;
+      // ---- epilogue: O_i / l -> 16-bit -> staging (128 x 32 boxes) -> TMA store
+#pragma unroll 1
+      for (int i = 0; i < 2; ++i) {
+        if ((i == 0 ? w.n[0] : w.n[1]) == 0 || !ok) continue;
+        ok = ws_wait(sh, smem_u32(&sh->o_full[i]), (phs >> (2 + i)) & 1u, p.status);
+        if (ok) ok = ws_wait(sh, smem_u32(&sh->fin[i]), (phs >> (4 + i)) & 1u, p.status);
+        if (!ok) break;
+        phs ^= (1u << (2 + i)) | (1u << (4 + i));
+        tc_fence_after();
+        const float inv = sh->inv_l[i][r];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sh->fin_free[i]));
+        const uint32_t tO = tmem + lane_off + G::TMEM_O + i * D;
+#pragma unroll 1
+        for (int q = 0; q < D / G::O_BOX_COLS; ++q) {
+          uint32_t pk[16];
+          {
+            uint32_t o[32];
+            tmem_ld32(tO + q * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+              pk[u] = pack2(__uint_as_float(o[2 * u]) * inv, __uint_as_float(o[2 * u + 1]) * inv,
+                            static_cast<T*>(nullptr));
+          }
+          if (q == D / G::O_BOX_COLS - 1) {
+            // O_i is read out: the next tile's first P V may overwrite it, and its step 0
+            // needs no rescale
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&sh->o_empty[i]));
+            const int t_next = t + t_step;
+            bool next_active = false;
+            if (t_next < p.total_tiles) {
+              const WsTile wn = ws_tile(p, t_next);
+              next_active = (i == 0 ? wn.n[0] : wn.n[1]) > 0;
+            }
+            if (next_active) {
+              if (lane == 0) mbar_arrive(smem_u32(&sh->p_ready[i]));
+              phs |= 1u << (10 + i);
+            }
+          }
+          // wait until this staging buffer's previous store has been read
+          ok = ws_wait(sh, smem_u32(&sh->ost_free[ostage]), ((phs >> (6 + ostage)) & 1u) ^ 1u,
+                       p.status);
+          if (!ok) break;
+          phs ^= 1u << (6 + ostage);
+          uint8_t* stg = o_stage + ostage * G::STAGE_BYTES;
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(stg + swizzle<G::O_SWZ>(r * G::O_SWZ + c * 16)) =
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&sh->ost_full[ostage]));
+          if (store_thread) {
+            // all four warps have written the box: store it; once the previous box's store
+            // has been read, that buffer is free again
+            if (!ws_wait1(sh, smem_u32(&sh->ost_full[ostage]), (phs >> (8 + ostage)) & 1u,
+                          p.status)) {
+              ok = false;
+            } else {
+              tma_store_4d(&tmO, smem_u32(stg), q * G::O_BOX_COLS, w.q0 + 128 * i, w.hi, w.bi);
+              bulk_commit_group();
+              bulk_wait_group_read1();
+              if (stores_issued) mbar_arrive(smem_u32(&sh->ost_free[ostage ^ 1]));
+              stores_issued = true;
+            }
+            phs ^= 1u << (8 + ostage);
+          }
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0 && ok;
+          if (!ok) break;
+          ostage ^= 1;
+        }
+      }
+    }
+    if (store_thread && stores_issued) bulk_wait_group_read0();
+  } else {
+    setmaxnreg_inc<G::REG_SOFTMAX>();
+    // ================================================================ softmax warpgroups
+    const int i = warp >> 2;   // query tile
+    const int wq = warp & 3;   // TMEM lane quarter
+    const int r = wq * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS = tmem + lane_off + G::TMEM_S + i * G::BN;
+    const float sl2 = p.scale_log2;
+    uint32_t sf_ph = 0;
+    uint32_t ff_ph = 0;  // inv_l slot: "free" phases (producer-style)
+    bool ok = true;
+    for (int t = t_first; t < p.total_tiles && ok; t += t_step) {
+      const WsTile w = ws_tile(p, t);
+      const int nk = w.n[i];
+      if (nk == 0) continue;
+      const int row = w.q0 + 128 * i + r;
+      float m = -INFINITY;  // exponent base, log2 units
+      float l = 0.f;
+      for (int j = 0; j < nk; ++j) {
+        ok = ws_wait(sh, smem_u32(&sh->s_full[i]), sf_ph, p.status);
+        if (!ok) break;
+        sf_ph ^= 1u;
+        tc_fence_after();
+        float s[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, reinterpret_cast<uint32_t*>(s) + c * 32);
+        tmem_wait_ld();
+
+        const int kv0 = j * 128;
+        const bool tail = kv0 + 128 > p.seqlen;
+        const bool diag = p.causal && (kv0 + 127 > w.q0 + 128 * i);
+        if (tail || diag) {
+          int lim = p.seqlen - kv0;
+          if (p.causal) lim = min(lim, row - kv0 + 1);
+#pragma unroll
+          for (int k = 0; k < 128; ++k)
+            if (k >= lim) s[k] = -INFINITY;
+        }
+        // row max -> exponent base; it moves only when the max passes it by more than 8
+        const float mx = row_max<128>(s) * sl2;
+        float acc = 1.f;
+        if (mx > m + RESCALE_LOG2) {
+          acc = ex2_approx(m - mx);  // m = -inf gives 0
+          m = mx;
+        }
+        if (j > 0) {
+          sh->acc_scale[i][r] = acc;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&sh->stats[i]));
+        }
+        const float neg_m = m == -INFINITY ? 0.f : -m;
+        const float2 sc = make_float2(sl2, sl2);
+        const float2 nm = make_float2(neg_m, neg_m);
+        // p = 2^(s * scale_log2 - m) in place; P to TMEM in four 32-key chunks
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const int k = c * 32 + 2 * u;
+            const float2 x = ffma2(make_float2(s[k], s[k + 1]), sc, nm);
+            float2 pr;
+            if (c >= 1 && c <= 2 && (u & 15) >= 16 - FA_WS_EMU_PAIRS) {
+              pr = exp2_poly2_deg3(x);
+            } else {
+              pr.x = ex2_approx(x.x);
+              pr.y = ex2_approx(x.y);
+            }
+            s[k] = pr.x;
+            s[k + 1] = pr.y;
+            pk[u] = pack2(pr.x, pr.y, static_cast<T*>(nullptr));
+          }
+          tmem_st16(tS + c * 16, pk);
+          if (c == 2 && FA_WS_SPLIT_P) {
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&sh->p_ready[i]));
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(FA_WS_SPLIT_P ? &sh->p_last[i] : &sh->p_ready[i]));
+        // row sum, off the path to the next MMA
+        float2 a4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) a4[u] = make_float2(s[2 * u], s[2 * u + 1]);
+#pragma unroll
+        for (int k = 8; k < 128; k += 8) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) a4[u] = fadd2(a4[u], make_float2(s[k + 2 * u], s[k + 2 * u + 1]));
+        }
+        const float2 a2 = fadd2(fadd2(a4[0], a4[1]), fadd2(a4[2], a4[3]));
+        l = l * acc + (a2.x + a2.y);
+      }
+      if (!ok) break;
+      // tile done: logsumexp, and 1/l for the correction warps' epilogue (once they have read
+      // the previous tile's)
+      if (row < p.seqlen) p.lse[static_cast<int64_t>(w.bh) * p.seqlen + row] = (m + log2f(l)) * kLn2;
+      ok = ws_wait(sh, smem_u32(&sh->fin_free[i]), ff_ph ^ 1u, p.status);
+      if (!ok) break;
+      ff_ph ^= 1u;
+      sh->inv_l[i][r] = 1.f / l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sh->fin[i]));
+    }
+  }
+
+  // ---- teardown: every thread arrives here exactly once
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 12) {
+    tc_fence_after();
+    tmem_dealloc(tmem, G::TMEM_ALLOC);
+  }
+}
+
+}  // namespace fa

@@ -7,6 +7,7 @@
 #include <cstdint>
 
 #include "fa_fwd_kernel.cuh"
+#include "fa_fwd_ws.cuh"
 
 namespace fa {
 
@@ -17,6 +18,8 @@ struct LaunchPlan {
   int block_n;  // 64 / 128
   int qt;       // query tiles per CTA (block_m / 128)
   bool vf8;     // V (and P) in float8 e5m2
+  bool ws;      // persistent warp-specialised kernel (fa_fwd_ws.cuh) instead of one CTA per tile
+  WsParams ws_params;
   int64_t grid;
   cudaStream_t stream;
 };
@@ -75,6 +78,41 @@ int launch_kernel(const LaunchPlan& lp) {
   kern<<<dim3(static_cast<unsigned>(lp.grid)), dim3(G::NUM_THREADS), smem, lp.stream>>>(
       lp.tmQ, lp.tmK, lp.tmV, lp.tmO, lp.params);
   return cudaGetLastError() == cudaSuccess ? 0 : -7;
+}
+
+// Launch the persistent kernel; lp.grid CTAs loop over lp.ws_params.total_tiles tiles.
+template <typename T, int D>
+int launch_ws(const LaunchPlan& lp) {
+  using G = WsGeo<T, D>;
+  auto kern = fa_fwd_ws_kernel<T, D>;
+  const int smem = ws_smem_bytes<D>(lp.ws_params.stages);
+  // The setmaxnreg split redistributes exactly the launch allocation (128 registers per thread
+  // for 512 threads); refuse a build whose per-thread count differs.
+  static int regs_ok = 0;  // 0 unknown, 1 ok, -1 mismatch
+  if (regs_ok == 0) {
+    cudaFuncAttributes fattr{};
+    regs_ok = (cudaFuncGetAttributes(&fattr, kern) == cudaSuccess && fattr.numRegs == 128) ? 1 : -1;
+    (void)cudaGetLastError();
+  }
+  if (regs_ok != 1) return -7;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess) {
+    (void)cudaGetLastError();
+    return -7;
+  }
+  kern<<<dim3(static_cast<unsigned>(lp.grid)), dim3(G::NUM_THREADS), smem, lp.stream>>>(
+      lp.tmQ, lp.tmK, lp.tmV, lp.tmO, lp.ws_params);
+  return cudaGetLastError() == cudaSuccess ? 0 : -7;
+}
+
+// Shared-memory footprint of the persistent kernel besides its K/V ring, and one ring stage.
+template <int D>
+constexpr int ws_smem_fixed() {
+  return ws_smem_bytes<D>(0);
+}
+template <int D>
+constexpr int ws_stage_bytes() {
+  return WsGeo<__nv_bfloat16, D>::KV_TILE_BYTES;
 }
 
 template <typename T, int D, int BN, int QT, bool VF8 = false>

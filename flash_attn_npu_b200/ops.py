@@ -124,7 +124,8 @@ def _tma_view(t: torch.Tensor) -> torch.Tensor:
 def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_scale: float, *,
             block_m: int = 0, block_n: int = 0, num_stages: int = 0, persistent_ctas: int = 0,
             out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
-            status: torch.Tensor | None = None, fp32_tf32: bool = False):
+            status: torch.Tensor | None = None, fp32_tf32: bool = False,
+            one_cta_per_tile: bool = False):
     """Run attention forward on the B200 kernel; returns (out, lse).
 
     `block_m/block_n/num_stages/persistent_ctas` = 0 picks the library default.  `out` and
@@ -134,7 +135,9 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_
     per-device word that `check_device_status()` reads.  float32 inputs run in fp32 on the
     CUDA cores unless `fp32_tf32` selects the (faster, TF32-rounded) tensor-core kernel.
     A float8_e5m2 `v` with float16/bfloat16 `q`, `k` runs the fp8-V kernel (P rounded to e5m2,
-    P.V on the fp8 tensor cores); `out` has q's dtype.
+    P.V on the fp8 tensor cores); `out` has q's dtype.  fp16/bf16 at head_dim 64/128 with the
+    256 x 128 tile run on the persistent kernel (grid `persistent_ctas`, 0 = one CTA per SM)
+    unless `one_cta_per_tile` asks for the other kernel.
     """
     validate_inputs(q, k, v)
     z, h, n_ctx, head_dim = q.shape
@@ -174,7 +177,8 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_
         persistent_ctas=persistent_ctas,
         status_ptr=(status.data_ptr() if status is not None else None),
         flags=((_native.FA_FLAG_FP32_TF32 if fp32_tf32 else 0)
-               | (_native.FA_FLAG_V_FP8_E5M2 if is_v_fp8(q, v) else 0)))
+               | (_native.FA_FLAG_V_FP8_E5M2 if is_v_fp8(q, v) else 0)
+               | (_native.FA_FLAG_ONE_CTA_PER_TILE if one_cta_per_tile else 0)))
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
         try:

@@ -12,7 +12,9 @@ Meaning of the knobs on sm_100a:
                    sharing each K/V tile, ping-ponged between two softmax warpgroups)
   BLOCK_N          keys per pipeline step: 64 or 128 (N of the Q.K^T MMA)
   NUM_STAGES       depth of the K/V shared-memory ring (each stage holds one K or one V tile)
-  PERSISTENT_CTAS  grid size cap; 0 = one CTA per tile
+  PERSISTENT_CTAS  grid of the persistent kernel (fp16/bf16, head_dim 64/128, 256 x 128): each
+                   CTA loops over tiles; 0 = one CTA per SM.  Other configurations run one
+                   CTA per tile and refuse a non-zero value.
 """
 from __future__ import annotations
 
@@ -64,12 +66,33 @@ def _elt_bytes(dtype) -> int:
     return 4 if dtype == torch.float32 else 2
 
 
+# Shared memory of the persistent kernel (csrc/fa_fwd_ws.cuh) besides its K/V ring: base
+# alignment, two query tiles, two 8 KiB output staging buffers and its barrier/statistics block.
+_WS_SHARED_BLOCK = 2384
+
+
+def persistent_kernel_serves(head_dim: int, dtype, cfg: TileConfig) -> bool:
+    """True when (dtype, head_dim, tile) runs on the persistent warp-specialised kernel: fp16 or
+    bf16, head_dim 64 or 128, BLOCK_M 256 and BLOCK_N 128 (with a positive softmax scale)."""
+    return (dtype in (torch.float16, torch.bfloat16) and head_dim in (64, 128)
+            and cfg.block_m == 256 and cfg.block_n == 128)
+
+
 def geometry(head_dim: int, dtype, cfg: TileConfig) -> dict | None:
-    """Shared-memory / TMEM footprint of one CTA, mirroring `Geo` in csrc/fa_fwd_kernel.cuh."""
+    """Shared-memory / TMEM footprint of one CTA, mirroring `Geo` in csrc/fa_fwd_kernel.cuh and
+    `WsGeo` in csrc/fa_fwd_ws.cuh."""
     eb = _elt_bytes(dtype)
     qt = cfg.block_m // 128
     if cfg.block_m not in BLOCK_M_CHOICES or cfg.block_n not in BLOCK_N_CHOICES:
         return None
+    if persistent_kernel_serves(head_dim, dtype, cfg):
+        q_tile = 128 * head_dim * eb
+        kv_tile = 128 * head_dim * eb
+        fixed = 1024 + 2 * q_tile + 2 * 8192 + _WS_SHARED_BLOCK
+        stages = min((SMEM_LIMIT - fixed) // kv_tile, MAX_STAGES)
+        return {"q_tile_bytes": q_tile, "kv_tile_bytes": kv_tile, "smem_fixed": fixed,
+                "max_stages": stages, "tmem_columns": 2 * (128 + head_dim), "threads": 512,
+                "persistent": True}
     tmem = qt * (cfg.block_n + head_dim)
     if tmem > TMEM_COLUMNS:
         return None
@@ -85,7 +108,8 @@ def geometry(head_dim: int, dtype, cfg: TileConfig) -> dict | None:
     if stages < 2:
         return None
     return {"q_tile_bytes": q_tile, "kv_tile_bytes": kv_tile, "smem_fixed": fixed,
-            "max_stages": stages, "tmem_columns": tmem, "threads": 128 + 128 * qt}
+            "max_stages": stages, "tmem_columns": tmem, "threads": 128 + 128 * qt,
+            "persistent": False}
 
 
 def is_supported(head_dim: int, dtype, cfg: TileConfig) -> bool:

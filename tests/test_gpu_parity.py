@@ -129,8 +129,13 @@ def test_ragged_sequence_lengths(seqlen, causal, cuda_device):
 
 @pytest.mark.parametrize("stages", [2, 3, 4, 5])
 def test_pipeline_depths(stages, cuda_device):
-    _run_and_check(1, 4, 1500, 128, torch.bfloat16, False, 256, 128, stages)
-    _run_and_check(1, 4, 1500, 128, torch.bfloat16, True, 256, 128, stages)
+    # 256 x 128 at head_dim 128 runs on the persistent kernel (ring depth <= 4); the
+    # one-CTA-per-tile kernel takes a 5-deep ring at the same tile
+    if stages <= 4:
+        _run_and_check(1, 4, 1500, 128, torch.bfloat16, False, 256, 128, stages)
+        _run_and_check(1, 4, 1500, 128, torch.bfloat16, True, 256, 128, stages)
+    _run_and_check(1, 4, 1500, 128, torch.bfloat16, False, 128, 128, stages)
+    _run_and_check(1, 4, 1500, 64, torch.float16, True, 256, 128, stages)
 
 
 @pytest.mark.parametrize("scale", [0.5, 1.0, -0.25, 0.0, 3.0])
@@ -351,3 +356,54 @@ def test_reference_evaluator_performance_shapes_at_preset_tiles(idx, dtype, cuda
         assert torch.allclose(ro.to(dtype), out[b, hh], atol=1e-2, rtol=1e-2)
     del q, k, v, out, lse
     torch.cuda.empty_cache()
+
+
+# ---------------------------------------------------------------- persistent kernel
+@pytest.mark.parametrize("ctas", [1, 3, 148, 5000])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_persistent_grid_sizes(head_dim, causal, ctas, cuda_device):
+    """The persistent kernel loops each CTA over tiles: any grid size gives the same result
+    (1 CTA walks every tile; more CTAs than tiles are trimmed to the tile count)."""
+    B, H, S = 2, 3, 1000
+    q = _rand((B, H, S, head_dim), torch.bfloat16, 40 + head_dim, "cuda")
+    k = _rand((B, H, S, head_dim), torch.bfloat16, 41 + head_dim, "cuda")
+    v = _rand((B, H, S, head_dim), torch.bfloat16, 42 + head_dim, "cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out, lse = ops.forward(q, k, v, causal, head_dim ** -0.5, block_m=256, block_n=128,
+                           persistent_ctas=ctas, status=status)
+    ro, rl = attention_ref_torch(q.cpu(), k.cpu(), v.cpu(), causal, head_dim ** -0.5)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    _check(out, lse, ro, rl)
+    ref_o, ref_l = ops.forward(q, k, v, causal, head_dim ** -0.5, block_m=256, block_n=128)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref_o) and torch.equal(lse, ref_l)  # same tiles, same arithmetic
+    assert ops.grid_size(B, H, S, head_dim, torch.bfloat16, causal, 256, 128) == min(
+        B * H * 4, torch.cuda.get_device_properties(0).multi_processor_count)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("causal", [False, True])
+def test_persistent_and_one_cta_per_tile_kernels_agree_with_oracle(dtype, causal, cuda_device):
+    B, H, S, D = 1, 4, 2100, 128
+    q, k, v = (_rand((B, H, S, D), dtype, s, "cuda") for s in (50, 51, 52))
+    ro, rl = attention_ref_torch(q.cpu(), k.cpu(), v.cpu(), causal, D ** -0.5)
+    o1, l1 = ops.forward(q, k, v, causal, D ** -0.5, block_m=256, block_n=128)
+    o2, l2 = ops.forward(q, k, v, causal, D ** -0.5, block_m=256, block_n=128,
+                         one_cta_per_tile=True)
+    torch.cuda.synchronize()
+    _check(o1, l1, ro, rl)
+    _check(o2, l2, ro, rl)
+    assert (o1.float() - o2.float()).abs().max().item() <= 2e-2
+
+
+def test_persistent_ctas_refused_where_one_cta_per_tile_runs(cuda_device):
+    q = _rand((1, 2, 300, 256), torch.bfloat16, 60, "cuda")
+    with pytest.raises(ValueError):
+        ops.forward(q, q, q, False, 0.1, persistent_ctas=20)            # head_dim 256
+    q64 = _rand((1, 2, 300, 64), torch.bfloat16, 61, "cuda")
+    with pytest.raises(ValueError):
+        ops.forward(q64, q64, q64, False, 0.1, block_m=128, block_n=128, persistent_ctas=20)
+    with pytest.raises(ValueError):
+        ops.forward(q64, q64, q64, False, -0.1, persistent_ctas=20)     # scale <= 0

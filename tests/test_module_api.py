@@ -72,13 +72,28 @@ def test_tiling_defaults_and_sources():
     rt = fam._describe_runtime(16, 16, 8192, 128, False)
     assert rt["selected_config"] == {"BLOCK_M": 256, "BLOCK_N": 128}
     assert rt["total_tiles"] == 32 * 256 and rt["stage"] == 1
-    assert rt["pipeline"]["NUM_STAGES"] == 5
+    # cfg4 runs on the persistent kernel: a 4-deep K/V ring, one CTA per SM looping over tiles
+    assert rt["pipeline"]["NUM_STAGES"] == 4
+    assert rt["kernel"] == "persistent"
+    assert rt["launched_programs"] == min(rt["total_tiles"], fam._sm_count())
     assert fam._build_grid(16, 16, 8192, 256) == (8192, 1, 1)
+    # head_dim 256 launches one CTA per tile
+    rt256 = fam._describe_runtime(1, 8, 2048, 256, False)
+    assert rt256["kernel"] == "one CTA per tile"
+    assert rt256["launched_programs"] == rt256["total_tiles"]
 
 
 def test_persistent_programs_env(monkeypatch):
     monkeypatch.setenv("PERSISTENT_PROGRAMS", "148")
     assert fam._get_persistent_programs() == 148
+    # it sizes the persistent kernel's grid ...
+    rt = fam._describe_runtime(4, 16, 4096, 128, True)
+    assert rt["pipeline"]["PERSISTENT_CTAS"] == 148 and rt["launched_programs"] == 148
+    monkeypatch.setenv("PERSISTENT_PROGRAMS", "20")
+    assert fam._describe_runtime(4, 16, 4096, 64, False)["launched_programs"] == 20
+    # ... and is refused, not silently dropped, where one CTA per tile is launched
+    with pytest.raises(ValueError, match="PERSISTENT_PROGRAMS"):
+        fam._describe_runtime(1, 8, 2048, 256, False)
     monkeypatch.setenv("PERSISTENT_PROGRAMS", "0")
     with pytest.raises(ValueError):
         fam._get_persistent_programs()
