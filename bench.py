@@ -173,6 +173,41 @@ def cpu_reference_rate(cfg, budget_s: float, q=None, k=None, v=None, rows=2048):
     return rate, desc, threads, t_total / done
 
 
+def library_rate(q, k, v, cfg, stream, steps):
+    """TFLOP/s of torch.nn.functional.scaled_dot_product_attention with the cuDNN backend on
+    the bench's own device inputs ([n, 1, S, D] slices), timed like the headline.  Context
+    only; None if the backend refuses the shape."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    try:
+        with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+            def run():
+                return F.scaled_dot_product_attention(q, k, v, is_causal=cfg.causal,
+                                                      scale=cfg.sm_scale)
+            for _ in range(3):
+                run()
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(steps):
+                run()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+    except Exception as exc:  # noqa: BLE001
+        return {"kernel": "torch sdpa (cuDNN)", "unavailable": type(exc).__name__}
+    flops = fa_flops_local(q, cfg)
+    return {"kernel": "torch.nn.functional.scaled_dot_product_attention, cuDNN backend",
+            "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms}
+
+
+def fa_flops_local(q, cfg):
+    n = q.shape[0] * q.shape[1]
+    f = 4.0 * n * cfg.seqlen * cfg.seqlen * cfg.head_dim
+    return f * 0.5 if cfg.causal else f
+
+
 # ----------------------------------------------------------------------------- arms
 def run_reference(args, cfg, world, rank):
     """Reference arm: the reference's CPU attention path on the host cores (rank 0 only)."""
@@ -400,6 +435,12 @@ def run_ours(args, cfg, world, rank, local):
                       "e2e_bitwise_equal_rank0": e2e_equal,
                       "gathered_with": "nccl p2p" if dist is not None else "local"}
 
+    # ---- context: the library attention kernel torch ships for this GPU (cuDNN through
+    # scaled_dot_product_attention), same inputs, same timing method (rank 0, N = 1 only)
+    library = None
+    if rank == 0 and world == 1 and not args.no_library:
+        library = library_rate(q, k, v, cfg, stream, args.steps)
+
     # ---- CPU baseline (rank 0, N = 1 only)
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -449,6 +490,7 @@ def run_ours(args, cfg, world, rank, local):
                          "kernel": "fa_fwd_sm100_kernel (one launch per step)"},
             "clocks": clocks,
             "cpu_baseline": cpu_baseline,
+            "context_library_kernel": library,
             "verify": verify,
         }
         print(json.dumps(line), flush=True)
@@ -476,6 +518,8 @@ def main(argv=None):
     ap.add_argument("--no-verify", action="store_true", dest="no_verify")
     ap.add_argument("--no-cpu-baseline", action="store_true", dest="no_cpu_baseline")
     ap.add_argument("--no-clocks", action="store_true", dest="no_clocks")
+    ap.add_argument("--no-library", action="store_true", dest="no_library",
+                    help="skip the context timing of torch's cuDNN attention kernel")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

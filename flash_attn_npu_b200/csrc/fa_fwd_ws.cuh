@@ -39,6 +39,8 @@
 // reaches exactly once.
 #pragma once
 
+#include <type_traits>
+
 #include "fa_fwd_kernel.cuh"
 
 namespace fa {
@@ -60,11 +62,6 @@ struct WsParams {
 // 2; chunk 0 and the last chunk use ex2.approx only.  6 -> 12 of 64 pairs (18.75 %).
 #ifndef FA_WS_EMU_PAIRS
 #define FA_WS_EMU_PAIRS 0
-#endif
-// Release P in two parts (first 96 keys, then the last 32) so the P.V MMAs start before the
-// softmax has finished the row.  0 releases the whole P at once.
-#ifndef FA_WS_SPLIT_P
-#define FA_WS_SPLIT_P 0
 #endif
 
 template <typename T, int D>
@@ -88,18 +85,18 @@ struct WsGeo {
   static constexpr int N_OSTAGE = 2;
   static constexpr int QK_MMAS = NBLK * (SWZ / 32);  // K = 16 elements = 32 bytes per MMA
   static constexpr int PV_MMAS = BN / 16;
-  static constexpr int PV_SPLIT = FA_WS_SPLIT_P ? 6 : PV_MMAS;  // MMAs on the first 96 keys
   static constexpr int TMEM_S = 0;
   static constexpr int TMEM_O = 2 * BN;
   static constexpr int TMEM_ALLOC = 512;
   static constexpr int NUM_THREADS = 512;
   // Register split: launched at 128 per thread (65536 / 512); the two softmax warpgroups
-  // take 184, the correction warpgroup 88, the producer/MMA warpgroup 56:
-  // 256 * 184 + 128 * 88 + 128 * 56 = 65536.
+  // take 192, the correction warpgroup 64, the producer/MMA warpgroup 64:
+  // 256 * 192 + 128 * 64 + 128 * 64 = 65536 (the split with the fewest spills; 184/88/56
+  // measured 3 % slower on cfg4).
 #ifndef FA_WS_REG_SOFTMAX
-#define FA_WS_REG_SOFTMAX 184
-#define FA_WS_REG_CORR 88
-#define FA_WS_REG_OTHER 56
+#define FA_WS_REG_SOFTMAX 192
+#define FA_WS_REG_CORR 64
+#define FA_WS_REG_OTHER 64
 #endif
   static constexpr int REG_SOFTMAX = FA_WS_REG_SOFTMAX;
   static constexpr int REG_CORR = FA_WS_REG_CORR;
@@ -115,9 +112,9 @@ struct WsShared {
   uint64_t q_full[2], q_empty[2];
   uint64_t kv_full[kMaxStages], kv_empty[kMaxStages];
   uint64_t s_full[2];   // MMA -> softmax: S_i(j) computed
-  uint64_t p_ready[2];  // softmax (first 3/4 of P) + correction (O rescaled) -> MMA
-  uint64_t p_last[2];   // softmax (last 1/4 of P) -> MMA
+  uint64_t p_ready[2];  // P_i(j) in TMEM and O_i rescaled -> MMA (see the softmax's release)
   uint64_t stats[2];    // softmax -> correction: acc_scale of step j >= 1 written
+  uint64_t stats_free[2];  // correction -> softmax: acc_scale read, it may be overwritten
   uint64_t fin[2];      // softmax -> correction: inv_l of the tile written
   uint64_t fin_free[2]; // correction -> softmax: inv_l read, the next tile may overwrite it
   uint64_t o_full[2];   // MMA -> correction: last P.V of the tile done
@@ -182,6 +179,7 @@ __device__ __forceinline__ bool ws_wait(WsShared* sh, uint32_t bar, uint32_t par
   return __all_sync(0xffffffffu, ws_wait1(sh, bar, parity, status));
 }
 
+
 template <typename T, int D>
 __global__ void __launch_bounds__(512, 1)
     fa_fwd_ws_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -210,9 +208,9 @@ __global__ void __launch_bounds__(512, 1)
       mbar_init(smem_u32(&sh->q_full[i]), 1);
       mbar_init(smem_u32(&sh->q_empty[i]), 1);
       mbar_init(smem_u32(&sh->s_full[i]), 1);
-      mbar_init(smem_u32(&sh->p_ready[i]), 8);  // 4 softmax warps + 4 correction warps
-      mbar_init(smem_u32(&sh->p_last[i]), 4);
+      mbar_init(smem_u32(&sh->p_ready[i]), 8);  // 2 per lane quarter (see the softmax's release)
       mbar_init(smem_u32(&sh->stats[i]), 4);
+      mbar_init(smem_u32(&sh->stats_free[i]), 4);
       mbar_init(smem_u32(&sh->fin[i]), 4);
       mbar_init(smem_u32(&sh->fin_free[i]), 4);
       mbar_init(smem_u32(&sh->o_full[i]), 1);
@@ -340,7 +338,6 @@ __global__ void __launch_bounds__(512, 1)
       const uint32_t empty0 = smem_u32(&sh->kv_empty[0]);
       const uint32_t s_bar = smem_u32(&sh->s_full[ti]);
       const uint32_t pr_bar = smem_u32(&sh->p_ready[ti]);
-      const uint32_t pl_bar = smem_u32(&sh->p_last[ti]);
       const uint32_t oe_bar = smem_u32(&sh->o_empty[ti]);
       const uint32_t qe_bar = smem_u32(&sh->q_empty[ti]);
       const uint32_t dS = tmem + G::TMEM_S + ti * G::BN;
@@ -375,7 +372,7 @@ __global__ void __launch_bounds__(512, 1)
         named_barrier_sync(ti == 0 ? kTok1 : kTok0, 64);
       };
 
-      // phase bits of this tile's barriers: q_full (0), p_ready (1), p_last (2), o_empty (3)
+      // phase bits of this tile's barriers: q_full (0), p_ready (1), o_empty (3)
       uint32_t phs = 0;
       int slot = 0;
       uint32_t ph = 0;
@@ -426,12 +423,6 @@ __global__ void __launch_bounds__(512, 1)
             ok = ws_wait(sh, oe_bar, ((phs >> 3) & 1u) ^ 1u, p.status);
             phs ^= 8u;
           }
-          if constexpr (G::PV_SPLIT < G::PV_MMAS) {
-            if (ok && act) {
-              ok = ws_wait(sh, pl_bar, (phs >> 2) & 1u, p.status);
-              phs ^= 4u;
-            }
-          }
           tc_fence_after();
           take_turn();
           if (ok && lead) {
@@ -465,37 +456,31 @@ __global__ void __launch_bounds__(512, 1)
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const bool store_thread = warp == 8 && lane == 0;
     // phase bits: stats (bit i), o_full (2 + i), fin (4 + i), staging free (6 + b, waited
-    // producer-style), staging written (8 + b, store thread); "step 0 already signalled" (10 + i)
+    // producer-style), staging written (8 + b, store thread)
     uint32_t phs = 0;
     int ostage = 0;
     bool ok = true;
     bool stores_issued = false;
 
-    auto arrive_p_ready = [&](int i) {
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sh->p_ready[i]));
-    };
-
     for (int t = t_first; t < p.total_tiles && ok; t += t_step) {
       const WsTile w = ws_tile(p, t);
-      for (int j = 0; j < w.n_max && ok; ++j) {
+      // Steps j >= 1: the softmax warp of this lane quarter hands over each row's rescale
+      // factor (1 when its exponent base stayed).  When one of the warp's 32 rows moved, the
+      // softmax released P_i(j) with one arrival and this warp adds the second once O_i is
+      // rescaled; otherwise the softmax's release already counted for both.
+      for (int j = 1; j < w.n_max && ok; ++j) {
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           if (j >= w.n[i] || !ok) continue;
-          if (j == 0) {
-            // step 0 starts O_i from zero: nothing to rescale
-            if (!((phs >> (10 + i)) & 1u)) arrive_p_ready(i);
-            phs &= ~(1u << (10 + i));
-            continue;
-          }
           ok = ws_wait(sh, smem_u32(&sh->stats[i]), (phs >> i) & 1u, p.status);
           if (!ok) break;
           phs ^= 1u << i;
           const float a = sh->acc_scale[i][r];
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&sh->stats_free[i]));
           if (__any_sync(0xffffffffu, a < 1.f)) {
             // O_i holds P V summed over steps < j (S_i(j) is complete, and the MMAs of one
-            // thread complete in order); rescale this warp's 32 rows
+            // thread complete in order) and P_i(j) V_j waits for this warp: rescale its rows
             tc_fence_after();
             const uint32_t tO = tmem + lane_off + G::TMEM_O + i * D;
 #pragma unroll 1
@@ -513,8 +498,10 @@ __global__ void __launch_bounds__(512, 1)
               tmem_st32(tO + c * 32, o);
             }
             tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&sh->p_ready[i]));
           }
-          arrive_p_ready(i);
         }
       }
       if (!ok) break;
@@ -544,21 +531,10 @@ __global__ void __launch_bounds__(512, 1)
                             static_cast<T*>(nullptr));
           }
           if (q == D / G::O_BOX_COLS - 1) {
-            // O_i is read out: the next tile's first P V may overwrite it, and its step 0
-            // needs no rescale
+            // O_i is read out: the next tile's first P V may overwrite it
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&sh->o_empty[i]));
-            const int t_next = t + t_step;
-            bool next_active = false;
-            if (t_next < p.total_tiles) {
-              const WsTile wn = ws_tile(p, t_next);
-              next_active = (i == 0 ? wn.n[0] : wn.n[1]) > 0;
-            }
-            if (next_active) {
-              if (lane == 0) mbar_arrive(smem_u32(&sh->p_ready[i]));
-              phs |= 1u << (10 + i);
-            }
           }
           // wait until this staging buffer's previous store has been read
           ok = ws_wait(sh, smem_u32(&sh->ost_free[ostage]), ((phs >> (6 + ostage)) & 1u) ^ 1u,
@@ -603,10 +579,62 @@ __global__ void __launch_bounds__(512, 1)
     const int r = wq * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t tS = tmem + lane_off + G::TMEM_S + i * G::BN;
+    const uint32_t pr_bar = smem_u32(&sh->p_ready[i]);
     const float sl2 = p.scale_log2;
-    uint32_t sf_ph = 0;
-    uint32_t ff_ph = 0;  // inv_l slot: "free" phases (producer-style)
+    const float2 sc = make_float2(sl2, sl2);
+    uint32_t sf_ph = 0;  // s_full
+    uint32_t xf_ph = 0;  // stats_free (producer-style)
+    uint32_t ff_ph = 0;  // fin_free (producer-style)
     bool ok = true;
+
+    // p = 2^(s * scale_log2 - m) for the row, P to TMEM in four 32-key chunks; returns the
+    // sum of the fp32 p.  s is left intact.
+    auto exp_pass = [&](const float* sv, float neg_m) -> float {
+      const float2 nm = make_float2(neg_m, neg_m);
+      float2 acc4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc4[u] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const int k = c * 32 + 2 * u;
+          const float2 x = ffma2(make_float2(sv[k], sv[k + 1]), sc, nm);
+          float2 pr;
+          if (c >= 1 && c <= 2 && u >= 16 - FA_WS_EMU_PAIRS) {
+            pr = exp2_poly2_deg3(x);
+          } else {
+            pr.x = ex2_approx(x.x);
+            pr.y = ex2_approx(x.y);
+          }
+          acc4[u & 3] = fadd2(acc4[u & 3], pr);
+          pk[u] = pack2(pr.x, pr.y, static_cast<T*>(nullptr));
+        }
+        tmem_st16(tS + c * 16, pk);
+      }
+      const float2 a2 = fadd2(fadd2(acc4[0], acc4[1]), fadd2(acc4[2], acc4[3]));
+      return a2.x + a2.y;
+    };
+    // Hands P_i(j) to the MMA warp: `count` arrivals of this warp on p_ready (2 = this lane
+    // quarter is complete; 1 = its correction warp adds the second after rescaling O).
+    auto release = [&](uint32_t count) {
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cnt(pr_bar, count);
+    };
+    // Hands this step's per-row rescale factors to the correction warp (once it has read the
+    // previous step's).
+    auto give_stats = [&](float acc) {
+      if (!ws_wait(sh, smem_u32(&sh->stats_free[i]), xf_ph ^ 1u, p.status)) return false;
+      xf_ph ^= 1u;
+      sh->acc_scale[i][r] = acc;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sh->stats[i]));
+      return true;
+    };
+
     for (int t = t_first; t < p.total_tiles && ok; t += t_step) {
       const WsTile w = ws_tile(p, t);
       const int nk = w.n[i];
@@ -623,7 +651,6 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, reinterpret_cast<uint32_t*>(s) + c * 32);
         tmem_wait_ld();
-
         const int kv0 = j * 128;
         const bool tail = kv0 + 128 > p.seqlen;
         const bool diag = p.causal && (kv0 + 127 > w.q0 + 128 * i);
@@ -634,63 +661,48 @@ __global__ void __launch_bounds__(512, 1)
           for (int k = 0; k < 128; ++k)
             if (k >= lim) s[k] = -INFINITY;
         }
-        // row max -> exponent base; it moves only when the max passes it by more than 8
-        const float mx = row_max<128>(s) * sl2;
-        float acc = 1.f;
-        if (mx > m + RESCALE_LOG2) {
-          acc = ex2_approx(m - mx);  // m = -inf gives 0
-          m = mx;
+        if (j == 0) {
+          // first key block: the exponent base is the row max (O starts from zero, so
+          // nothing is rescaled and the correction warps are not involved)
+          m = row_max<128>(s) * sl2;
+          const float sum = exp_pass(s, m == -INFINITY ? 0.f : -m);
+          release(2u);
+          l = sum;
+          continue;
         }
-        if (j > 0) {
-          sh->acc_scale[i][r] = acc;
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&sh->stats[i]));
-        }
-        const float neg_m = m == -INFINITY ? 0.f : -m;
-        const float2 sc = make_float2(sl2, sl2);
-        const float2 nm = make_float2(neg_m, neg_m);
-        // p = 2^(s * scale_log2 - m) in place; P to TMEM in four 32-key chunks
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const int k = c * 32 + 2 * u;
-            const float2 x = ffma2(make_float2(s[k], s[k + 1]), sc, nm);
-            float2 pr;
-            if (c >= 1 && c <= 2 && (u & 15) >= 16 - FA_WS_EMU_PAIRS) {
-              pr = exp2_poly2_deg3(x);
-            } else {
-              pr.x = ex2_approx(x.x);
-              pr.y = ex2_approx(x.y);
+        {
+          // Optimistic pass: exponentiate against the current base, row sum in the same pass.
+          // Every p <= 2^RESCALE_LOG2 whenever the row's sum is; only a row whose sum exceeds
+          // P_SUM_BOUND (always one whose max moved past base + RESCALE_LOG2, rarely any other
+          // once the base has settled) takes the row max, and a warp with a row that needs the
+          // new base recomputes P.  The decisions are those of a max taken every step.  A
+          // warp whose rows all keep their base releases P on its own; otherwise its correction
+          // warp rescales O and adds the second arrival.
+          float sum = exp_pass(s, m == -INFINITY ? 0.f : -m);
+          float acc = 1.f;
+          bool any_need = false;
+          if (__any_sync(0xffffffffu, !(sum <= P_SUM_BOUND) || m == -INFINITY)) {
+            const float mx = row_max<128>(s) * sl2;
+            const bool need = mx > m + RESCALE_LOG2;
+            any_need = __any_sync(0xffffffffu, need);
+            if (any_need) {
+              if (need) {
+                acc = ex2_approx(m - mx);  // m = -inf gives 0
+                m = mx;
+              }
+              ok = give_stats(acc);
+              if (!ok) break;
+              tmem_wait_st();  // the first pass's P stores land before they are overwritten
+              sum = exp_pass(s, m == -INFINITY ? 0.f : -m);
             }
-            s[k] = pr.x;
-            s[k + 1] = pr.y;
-            pk[u] = pack2(pr.x, pr.y, static_cast<T*>(nullptr));
           }
-          tmem_st16(tS + c * 16, pk);
-          if (c == 2 && FA_WS_SPLIT_P) {
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&sh->p_ready[i]));
+          release(any_need ? 1u : 2u);
+          l = l * acc + sum;
+          if (!any_need) {
+            ok = give_stats(1.f);
+            if (!ok) break;
           }
         }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(FA_WS_SPLIT_P ? &sh->p_last[i] : &sh->p_ready[i]));
-        // row sum, off the path to the next MMA
-        float2 a4[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) a4[u] = make_float2(s[2 * u], s[2 * u + 1]);
-#pragma unroll
-        for (int k = 8; k < 128; k += 8) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u) a4[u] = fadd2(a4[u], make_float2(s[k + 2 * u], s[k + 2 * u + 1]));
-        }
-        const float2 a2 = fadd2(fadd2(a4[0], a4[1]), fadd2(a4[2], a4[3]));
-        l = l * acc + (a2.x + a2.y);
       }
       if (!ok) break;
       // tile done: logsumexp, and 1/l for the correction warps' epilogue (once they have read
