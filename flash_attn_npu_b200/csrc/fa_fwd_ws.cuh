@@ -63,6 +63,11 @@ struct WsParams {
 #ifndef FA_WS_EMU_PAIRS
 #define FA_WS_EMU_PAIRS 0
 #endif
+// 1: after its first base move past the first key block, a softmax warp takes the row max
+// first for the rest of the tile (see the softmax); 0: optimistic throughout.
+#ifndef FA_WS_ADAPTIVE
+#define FA_WS_ADAPTIVE 1
+#endif
 
 template <typename T, int D>
 struct WsGeo {
@@ -642,12 +647,12 @@ __global__ void __launch_bounds__(512, 1)
       const int row = w.q0 + 128 * i + r;
       float m = -INFINITY;  // exponent base, log2 units
       float l = 0.f;
-      for (int j = 0; j < nk; ++j) {
-        ok = ws_wait(sh, smem_u32(&sh->s_full[i]), sf_ph, p.status);
-        if (!ok) break;
+      float s[128];
+      // S_i(j) into registers, keys past the sequence end / above the diagonal at -inf
+      auto load_s = [&](int j) -> bool {
+        if (!ws_wait(sh, smem_u32(&sh->s_full[i]), sf_ph, p.status)) return false;
         sf_ph ^= 1u;
         tc_fence_after();
-        float s[128];
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, reinterpret_cast<uint32_t*>(s) + c * 32);
         tmem_wait_ld();
@@ -661,47 +666,80 @@ __global__ void __launch_bounds__(512, 1)
           for (int k = 0; k < 128; ++k)
             if (k >= lim) s[k] = -INFINITY;
         }
-        if (j == 0) {
-          // first key block: the exponent base is the row max (O starts from zero, so
-          // nothing is rescaled and the correction warps are not involved)
-          m = row_max<128>(s) * sl2;
-          const float sum = exp_pass(s, m == -INFINITY ? 0.f : -m);
-          release(2u);
-          l = sum;
-          continue;
-        }
-        {
-          // Optimistic pass: exponentiate against the current base, row sum in the same pass.
-          // Every p <= 2^RESCALE_LOG2 whenever the row's sum is; only a row whose sum exceeds
-          // P_SUM_BOUND (always one whose max moved past base + RESCALE_LOG2, rarely any other
-          // once the base has settled) takes the row max, and a warp with a row that needs the
-          // new base recomputes P.  The decisions are those of a max taken every step.  A
-          // warp whose rows all keep their base releases P on its own; otherwise its correction
-          // warp rescales O and adds the second arrival.
-          float sum = exp_pass(s, m == -INFINITY ? 0.f : -m);
-          float acc = 1.f;
-          bool any_need = false;
-          if (__any_sync(0xffffffffu, !(sum <= P_SUM_BOUND) || m == -INFINITY)) {
-            const float mx = row_max<128>(s) * sl2;
-            const bool need = mx > m + RESCALE_LOG2;
-            any_need = __any_sync(0xffffffffu, need);
-            if (any_need) {
-              if (need) {
-                acc = ex2_approx(m - mx);  // m = -inf gives 0
-                m = mx;
-              }
-              ok = give_stats(acc);
-              if (!ok) break;
-              tmem_wait_st();  // the first pass's P stores land before they are overwritten
-              sum = exp_pass(s, m == -INFINITY ? 0.f : -m);
+        return true;
+      };
+      // ---- first key block: the exponent base is the row max (O starts from zero, so nothing
+      // is rescaled and the correction warps are not involved)
+      ok = load_s(0);
+      if (!ok) break;
+      m = row_max<128>(s) * sl2;
+      l = exp_pass(s, m == -INFINITY ? 0.f : -m);
+      release(2u);
+      // ---- later blocks, optimistic: exponentiate against the current base with the row sum
+      // in the same pass.  Every p <= 2^RESCALE_LOG2 whenever the row's sum is; only a row
+      // whose sum exceeds P_SUM_BOUND (always one whose max moved past base + RESCALE_LOG2,
+      // rarely any other once the base has settled) takes the row max, and a warp with a row
+      // that needs the new base recomputes P.  A warp whose rows all keep their base releases
+      // P on its own; otherwise its correction warp rescales O and adds the second arrival.
+      // The first base move after the first block ends this loop for the tile: rows whose max
+      // keeps moving (outlier-heavy inputs) would otherwise pay a second exponent pass per
+      // move, so the rest of the tile takes the max first.
+      int j = 1;
+      for (; j < nk; ++j) {
+        ok = load_s(j);
+        if (!ok) break;
+        float sum = exp_pass(s, m == -INFINITY ? 0.f : -m);
+        float acc = 1.f;
+        bool any_need = false;
+        if (__any_sync(0xffffffffu, !(sum <= P_SUM_BOUND) || m == -INFINITY)) {
+          const float mx = row_max<128>(s) * sl2;
+          const bool need = mx > m + RESCALE_LOG2;
+          any_need = __any_sync(0xffffffffu, need);
+          if (any_need) {
+            if (need) {
+              acc = ex2_approx(m - mx);  // m = -inf gives 0
+              m = mx;
             }
-          }
-          release(any_need ? 1u : 2u);
-          l = l * acc + sum;
-          if (!any_need) {
-            ok = give_stats(1.f);
+            ok = give_stats(acc);
             if (!ok) break;
+            tmem_wait_st();  // the first pass's P stores land before they are overwritten
+            sum = exp_pass(s, m == -INFINITY ? 0.f : -m);
           }
+        }
+        release(any_need ? 1u : 2u);
+        l = l * acc + sum;
+        if (!any_need) {
+          ok = give_stats(1.f);
+          if (!ok) break;
+        } else if (FA_WS_ADAPTIVE) {
+          ++j;
+          break;
+        }
+      }
+      if (!ok) break;
+      // ---- the rest of the tile: row max first, then the exponentials against the chosen
+      // base; a base move costs the correction warp's O rescale, overlapped with this pass
+      for (; j < nk; ++j) {
+        ok = load_s(j);
+        if (!ok) break;
+        const float mx = row_max<128>(s) * sl2;
+        const bool need = mx > m + RESCALE_LOG2;
+        float acc = 1.f;
+        if (need) {
+          acc = ex2_approx(m - mx);  // m = -inf gives 0
+          m = mx;
+        }
+        const bool any_need = __any_sync(0xffffffffu, need);
+        if (any_need) {
+          ok = give_stats(acc);
+          if (!ok) break;
+        }
+        const float sum = exp_pass(s, m == -INFINITY ? 0.f : -m);
+        release(any_need ? 1u : 2u);
+        l = l * acc + sum;
+        if (!any_need) {
+          ok = give_stats(1.f);
+          if (!ok) break;
         }
       }
       if (!ok) break;
