@@ -176,7 +176,7 @@ def cpu_reference_rate(cfg, budget_s: float, q=None, k=None, v=None, rows=2048):
 def library_rate(q, k, v, cfg, stream, steps):
     """TFLOP/s of torch.nn.functional.scaled_dot_product_attention with the cuDNN backend on
     the bench's own device inputs ([n, 1, S, D] slices), timed like the headline.  Context
-    only; None if the backend refuses the shape."""
+    only; {"unavailable": ...} if the backend refuses the shape."""
     import torch.nn.functional as F
     from torch.nn.attention import SDPBackend, sdpa_kernel
     try:
@@ -200,6 +200,16 @@ def library_rate(q, k, v, cfg, stream, steps):
     flops = fa_flops_local(q, cfg)
     return {"kernel": "torch.nn.functional.scaled_dot_product_attention, cuDNN backend",
             "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms}
+
+
+def kernel_label(cfg, fam):
+    """Which kernel the workload's default tile runs on (one launch per step either way)."""
+    from flash_attn_npu_b200 import tiling
+    tc = tiling.TileConfig.from_preset(fam.get_tile_config(cfg.batch, cfg.heads, cfg.seqlen,
+                                                          cfg.head_dim, cfg.causal, cfg.dtype))
+    if tiling.persistent_kernel_serves(cfg.head_dim, cfg.dtype, tc) and cfg.sm_scale > 0:
+        return "fa_fwd_ws_kernel (persistent, one launch per step)"
+    return "fa_fwd_sm100_kernel (one CTA per tile, one launch per step)"
 
 
 def fa_flops_local(q, cfg):
@@ -487,7 +497,7 @@ def run_ours(args, cfg, world, rank, local):
                          "frac_sustained": achieved / peaks["bf16_tflops_sustained"],
                          "peak_source": f"{peak_src} bf16 dense (burst)",
                          "traffic": traffic,
-                         "kernel": "fa_fwd_sm100_kernel (one launch per step)"},
+                         "kernel": kernel_label(cfg, fam)},
             "clocks": clocks,
             "cpu_baseline": cpu_baseline,
             "context_library_kernel": library,

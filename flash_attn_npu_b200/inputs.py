@@ -60,6 +60,23 @@ CONFIGS = {
                        "outliers"),
 }
 
+# Sequence lengths that are not a multiple of the 128-key block, beside their tile-multiple
+# neighbours (the reference drops the keys past the last full block, flash_attention_forward.py
+# :846-869, and asserts N_CTX % BLOCK_M == 0, :976; these measure what the masked tails cost).
+RAGGED_CONFIGS = {
+    "cfg4_s8191": AttnConfig("cfg4_s8191", 16, 16, 8191, 128, torch.bfloat16, False, 3,
+                             1 / math.sqrt(128), "randn"),
+    "causal_s1024": AttnConfig("causal_s1024", 64, 16, 1024, 128, torch.bfloat16, True, 5,
+                               1 / math.sqrt(128), "randn"),
+    "causal_s1000": AttnConfig("causal_s1000", 64, 16, 1000, 128, torch.bfloat16, True, 5,
+                               1 / math.sqrt(128), "randn"),
+    "causal_s2048": AttnConfig("causal_s2048", 32, 16, 2048, 128, torch.bfloat16, True, 6,
+                               1 / math.sqrt(128), "randn"),
+    "causal_s2049": AttnConfig("causal_s2049", 32, 16, 2049, 128, torch.bfloat16, True, 6,
+                               1 / math.sqrt(128), "randn"),
+}
+CONFIGS.update(RAGGED_CONFIGS)
+
 HEADLINE = "cfg4"
 
 
