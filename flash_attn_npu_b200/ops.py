@@ -195,7 +195,7 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_
 
 
 def grid_size(z: int, h: int, n_ctx: int, head_dim: int, dtype: torch.dtype, causal: bool,
-              block_m: int = 0, block_n: int = 0) -> int:
+              block_m: int = 0, block_n: int = 0, persistent_ctas: int = 0) -> int:
     """CTAs one launch uses (no device needed)."""
     args = _native.make_args(
         q_ptr=16, k_ptr=16, v_ptr=16, o_ptr=16, lse_ptr=16, batch=z, heads=h, seqlen=n_ctx,
@@ -203,5 +203,6 @@ def grid_size(z: int, h: int, n_ctx: int, head_dim: int, dtype: torch.dtype, cau
         k_stride=(h * n_ctx * head_dim, n_ctx * head_dim, head_dim),
         v_stride=(h * n_ctx * head_dim, n_ctx * head_dim, head_dim),
         o_stride=(h * n_ctx * head_dim, n_ctx * head_dim, head_dim), dtype_code=dtype_code(dtype),
-        causal=causal, sm_scale=1.0, block_m=block_m, block_n=block_n)
+        causal=causal, sm_scale=1.0, block_m=block_m, block_n=block_n,
+        persistent_ctas=persistent_ctas)
     return _native.grid_size(args)

@@ -12,9 +12,11 @@ Meaning of the knobs on sm_100a:
                    sharing each K/V tile, ping-ponged between two softmax warpgroups)
   BLOCK_N          keys per pipeline step: 64 or 128 (N of the Q.K^T MMA)
   NUM_STAGES       depth of the K/V shared-memory ring (each stage holds one K or one V tile)
-  PERSISTENT_CTAS  grid of the persistent kernel (fp16/bf16, head_dim 64/128, 256 x 128): each
-                   CTA loops over tiles; 0 = one CTA per SM.  Other configurations run one
-                   CTA per tile and refuse a non-zero value.
+  PERSISTENT_CTAS  > 0: run the persistent kernel (fp16/bf16, head_dim 64/128, 256 x 128) on a
+                   grid of that many CTAs, each looping over tiles.  0: library default --
+                   the persistent kernel (one CTA per SM) for causal masks, one CTA per tile
+                   otherwise.  Configurations the persistent kernel does not serve refuse a
+                   non-zero value.
 """
 from __future__ import annotations
 
@@ -71,11 +73,19 @@ def _elt_bytes(dtype) -> int:
 _WS_SHARED_BLOCK = 2384
 
 
-def persistent_kernel_serves(head_dim: int, dtype, cfg: TileConfig) -> bool:
-    """True when (dtype, head_dim, tile) runs on the persistent warp-specialised kernel: fp16 or
-    bf16, head_dim 64 or 128, BLOCK_M 256 and BLOCK_N 128 (with a positive softmax scale)."""
+def persistent_kernel_shape(head_dim: int, dtype, cfg: TileConfig) -> bool:
+    """True when the persistent warp-specialised kernel can serve (dtype, head_dim, tile):
+    fp16 or bf16, head_dim 64 or 128, BLOCK_M 256 and BLOCK_N 128."""
     return (dtype in (torch.float16, torch.bfloat16) and head_dim in (64, 128)
             and cfg.block_m == 256 and cfg.block_n == 128)
+
+
+def persistent_kernel_serves(head_dim: int, dtype, cfg: TileConfig, causal: bool,
+                             sm_scale: float = 1.0) -> bool:
+    """True when a call runs on the persistent kernel (mirrors `use_ws` in csrc/fa_fwd_api.cu):
+    a shape it serves, a positive scale, and either PERSISTENT_CTAS > 0 or a causal mask."""
+    return (persistent_kernel_shape(head_dim, dtype, cfg) and sm_scale > 0
+            and (cfg.persistent_ctas > 0 or bool(causal)))
 
 
 def geometry(head_dim: int, dtype, cfg: TileConfig) -> dict | None:
@@ -85,7 +95,7 @@ def geometry(head_dim: int, dtype, cfg: TileConfig) -> dict | None:
     qt = cfg.block_m // 128
     if cfg.block_m not in BLOCK_M_CHOICES or cfg.block_n not in BLOCK_N_CHOICES:
         return None
-    if persistent_kernel_serves(head_dim, dtype, cfg):
+    if persistent_kernel_shape(head_dim, dtype, cfg):
         q_tile = 128 * head_dim * eb
         kv_tile = 128 * head_dim * eb
         fixed = 1024 + 2 * q_tile + 2 * 8192 + _WS_SHARED_BLOCK

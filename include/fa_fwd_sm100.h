@@ -47,8 +47,8 @@ enum FaDtype { FA_DTYPE_FP16 = 0, FA_DTYPE_BF16 = 1, FA_DTYPE_FP32 = 2 };
  * P.V runs on the fp8 tensor-core path.  Replaces the reference's fp8_v mode
  * (flash_attention_forward.py:704, :996: taken when V is float8e5). */
 /* FA_FLAG_ONE_CTA_PER_TILE: run the one-CTA-per-query-block kernel even where the persistent
- * kernel would serve the call (fp16 / bf16, head_dim 64 or 128, block 256 x 128, sm_scale > 0);
- * kept for A/B comparisons of the two kernels. */
+ * kernel would serve the call (see FaTileConfig.persistent_ctas); kept for A/B comparisons of
+ * the two kernels. */
 enum FaFlags { FA_FLAG_FP32_TF32 = 1, FA_FLAG_V_FP8_E5M2 = 2, FA_FLAG_ONE_CTA_PER_TILE = 4 };
 
 /* Return codes. */
@@ -69,10 +69,12 @@ typedef struct FaTileConfig {
   int32_t block_m;         /* query rows per CTA: 128 or 256 (two 128-row tiles) */
   int32_t block_n;         /* keys per pipeline step: 64 or 128 */
   int32_t num_stages;      /* K/V shared-memory ring depth; 0 = largest that fits */
-  int32_t persistent_ctas; /* CTAs of the persistent kernel's grid (each loops over tiles,
-                              reference PERSISTENT_PROGRAMS); 0 = one per SM.  Non-zero values
-                              are refused (FA_ERR_UNSUPPORTED_TILE) for configurations that run
-                              one CTA per tile. */
+  int32_t persistent_ctas; /* > 0: run the persistent kernel with a grid of this many CTAs,
+                              each looping over tiles (reference PERSISTENT_PROGRAMS); refused
+                              (FA_ERR_UNSUPPORTED_TILE) where that kernel does not serve the call
+                              (it serves fp16 / bf16, head_dim 64 / 128, block 256 x 128,
+                              sm_scale > 0).  0: library default -- the persistent kernel with
+                              one CTA per SM for causal masks, one CTA per tile otherwise. */
 } FaTileConfig;
 
 typedef struct FaFwdArgs {

@@ -376,11 +376,17 @@ def test_persistent_grid_sizes(head_dim, causal, ctas, cuda_device):
     torch.cuda.synchronize()
     assert status.item() == 0
     _check(out, lse, ro, rl)
-    ref_o, ref_l = ops.forward(q, k, v, causal, head_dim ** -0.5, block_m=256, block_n=128)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    ref_o, ref_l = ops.forward(q, k, v, causal, head_dim ** -0.5, block_m=256, block_n=128,
+                               persistent_ctas=sms)
     torch.cuda.synchronize()
     assert torch.equal(out, ref_o) and torch.equal(lse, ref_l)  # same tiles, same arithmetic
-    assert ops.grid_size(B, H, S, head_dim, torch.bfloat16, causal, 256, 128) == min(
-        B * H * 4, torch.cuda.get_device_properties(0).multi_processor_count)
+    tiles = B * H * 4
+    assert ops.grid_size(B, H, S, head_dim, torch.bfloat16, causal, 256, 128, ctas) == min(
+        tiles, ctas)
+    # library default: persistent (one CTA per SM) for causal masks, one CTA per tile otherwise
+    assert ops.grid_size(B, H, S, head_dim, torch.bfloat16, causal, 256, 128) == (
+        min(tiles, sms) if causal else tiles)
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
@@ -389,7 +395,9 @@ def test_persistent_and_one_cta_per_tile_kernels_agree_with_oracle(dtype, causal
     B, H, S, D = 1, 4, 2100, 128
     q, k, v = (_rand((B, H, S, D), dtype, s, "cuda") for s in (50, 51, 52))
     ro, rl = attention_ref_torch(q.cpu(), k.cpu(), v.cpu(), causal, D ** -0.5)
-    o1, l1 = ops.forward(q, k, v, causal, D ** -0.5, block_m=256, block_n=128)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    o1, l1 = ops.forward(q, k, v, causal, D ** -0.5, block_m=256, block_n=128,
+                         persistent_ctas=sms)
     o2, l2 = ops.forward(q, k, v, causal, D ** -0.5, block_m=256, block_n=128,
                          one_cta_per_tile=True)
     torch.cuda.synchronize()
