@@ -207,7 +207,7 @@ def kernel_label(cfg, fam):
     from flash_attn_npu_b200 import tiling
     tc = tiling.TileConfig.from_preset(fam.get_tile_config(cfg.batch, cfg.heads, cfg.seqlen,
                                                           cfg.head_dim, cfg.causal, cfg.dtype))
-    if tiling.persistent_kernel_serves(cfg.head_dim, cfg.dtype, tc, cfg.causal, cfg.sm_scale):
+    if tiling.persistent_kernel_serves(cfg.head_dim, cfg.dtype, tc, cfg.sm_scale):
         return "fa_fwd_ws_kernel (persistent, one launch per step)"
     return "fa_fwd_sm100_kernel (one CTA per tile, one launch per step)"
 

@@ -32,9 +32,8 @@ from flash_attn_npu_b200 import tiling as _tiling
 DEVICE = "cuda"
 RESULT_DIR_NAME = "result_dir"
 # PERSISTENT_PROGRAMS (reference default: 20 programs = 20 Ascend cores) sizes the persistent
-# kernel's grid (float16/bfloat16, HEAD_DIM 64/128, 256 x 128 tiles) and selects that kernel;
-# 0 leaves the choice to the library (persistent with one CTA per SM for causal masks, one CTA
-# per tile otherwise).
+# kernel's grid (float16/bfloat16, HEAD_DIM 64/128, 256 x 128 tiles); 0 means one CTA per SM.
+# Other configurations launch one CTA per tile and refuse a non-zero value.
 DEFAULT_PERSISTENT_PROGRAMS = 0
 PROFILE_OP_NAME = "fa_fwd_sm100_kernel"
 
@@ -132,7 +131,7 @@ def _sm_count():
 def _describe_runtime(z, h, n_ctx, head_dim, causal, bm=None, bn=None, dtype=torch.bfloat16):
     cfg, tiling_source = _resolve_config(z, h, n_ctx, head_dim, causal, dtype, bm, bn)
     total_tiles = -(-n_ctx // cfg.block_m) * z * h
-    persistent = _tiling.persistent_kernel_serves(head_dim, dtype, cfg, causal)
+    persistent = _tiling.persistent_kernel_serves(head_dim, dtype, cfg)
     # the persistent kernel's grid is PERSISTENT_CTAS (0: one CTA per SM), each CTA looping
     # over tiles; every other configuration launches one CTA per tile
     launched = (min(total_tiles, cfg.persistent_ctas or _sm_count()) if persistent

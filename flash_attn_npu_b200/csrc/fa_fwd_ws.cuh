@@ -25,18 +25,20 @@
 // One KV step j, per tile i, issued by tile i's MMA warp in its turn, once P_i(j) is in TMEM
 // and the correction warps have rescaled O_i:
 //   O_i (+)= P_i V_j ;  S_i = Q_i K_{j+1}^T  (commit: S_i full)
-// The softmax warpgroup of tile i, per step: load S_i, row max, pick the exponent base
-// (it moves only when the row max passes it by more than 8 in log2 units, so O and l rarely
-// need rescaling), hand the per-row rescale factor to the correction warps, exponentiate
-// (ex2.approx, with a fixed minority of element pairs on the FMA pipe), store P_i in four
-// 32-key chunks -- the first three released together, the last one on its own -- and only
-// then add the row sum, which is off the path to the next MMA.
+// The softmax warpgroup of tile i, per step: load S_i (the upper half still loading while the
+// lower half is exponentiated), exponentiate against the row's exponent base (ex2.approx,
+// packed f32x2 arithmetic) with the row sum in the same pass, store P_i over S_i as packed
+// 16-bit pairs and release it.  The base moves only when the row max passes it by more than 8
+// in log2 units, so O and l rarely need rescaling; the max is taken only when the row sum
+// shows it may have moved (see the softmax), and a move hands the per-row rescale factor to
+// the correction warps, which rescale O_i in TMEM before the next P V.
 //
 // Every wait is bounded (FA_WAIT_TIMEOUT_NS); a wait that gives up records
 // FA_ERR_DEVICE_TIMEOUT in the status word and raises the CTA's abort flag, after which every
 // role leaves its loop and drains what it has in flight (FA_DRAIN_TIMEOUT_NS) before TMEM is
-// freed.  The only unbounded synchronisation is the final __syncthreads, which every thread
-// reaches exactly once.
+// freed.  The unbounded synchronisations are the final __syncthreads, which every thread
+// reaches exactly once, and the two issuers' turn-taking named barriers, which both pass the
+// same number of times on every path (a wait that gives up only stops the issuing).
 #pragma once
 
 #include <type_traits>
@@ -594,13 +596,21 @@ __global__ void __launch_bounds__(512, 1)
 
     // p = 2^(s * scale_log2 - m) for the row, P to TMEM in four 32-key chunks; returns the
     // sum of the fp32 p.  s is left intact.
-    auto exp_pass = [&](const float* sv, float neg_m) -> float {
+    // With `upper_in_flight`, the upper 64 logits are still being loaded from TMEM (see
+    // load_s_lower) and are waited for once the lower half has been exponentiated.
+    auto exp_pass = [&](float* sv, float neg_m, bool upper_in_flight = false) -> float {
       const float2 nm = make_float2(neg_m, neg_m);
       float2 acc4[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) acc4[u] = make_float2(0.f, 0.f);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
+        if (c == 2 && upper_in_flight) {
+          tmem_wait_ld();
+          // the registers the asynchronous load wrote are read only after the wait
+#pragma unroll
+          for (int k = 64; k < 128; ++k) asm volatile("" : "+f"(sv[k]));
+        }
         uint32_t pk[16];
 #pragma unroll
         for (int u = 0; u < 16; ++u) {
@@ -668,6 +678,31 @@ __global__ void __launch_bounds__(512, 1)
         }
         return true;
       };
+      // S_i(j) for the optimistic pass: on an unmasked step only the lower 64 logits are
+      // waited for, the upper 64 load while the lower half is exponentiated (true); a masked
+      // step (causal diagonal, sequence tail) loads and masks the whole row (false).  Sets
+      // `ok` to false on a timeout.
+      auto load_s_lower = [&](int j) -> bool {
+        const int kv0 = j * 128;
+        const bool tail = kv0 + 128 > p.seqlen;
+        const bool diag = p.causal && (kv0 + 127 > w.q0 + 128 * i);
+        if (tail || diag) {
+          ok = load_s(j);
+          return false;
+        }
+        ok = ws_wait(sh, smem_u32(&sh->s_full[i]), sf_ph, p.status);
+        if (!ok) return false;
+        sf_ph ^= 1u;
+        tc_fence_after();
+        tmem_ld32(tS, reinterpret_cast<uint32_t*>(s));
+        tmem_ld32(tS + 32, reinterpret_cast<uint32_t*>(s) + 32);
+        tmem_wait_ld();
+#pragma unroll
+        for (int k = 0; k < 64; ++k) asm volatile("" : "+f"(s[k]));
+        tmem_ld32(tS + 64, reinterpret_cast<uint32_t*>(s) + 64);
+        tmem_ld32(tS + 96, reinterpret_cast<uint32_t*>(s) + 96);
+        return true;
+      };
       // ---- first key block: the exponent base is the row max (O starts from zero, so nothing
       // is rescaled and the correction warps are not involved)
       ok = load_s(0);
@@ -686,9 +721,9 @@ __global__ void __launch_bounds__(512, 1)
       // move, so the rest of the tile takes the max first.
       int j = 1;
       for (; j < nk; ++j) {
-        ok = load_s(j);
+        const bool upper_in_flight = load_s_lower(j);
         if (!ok) break;
-        float sum = exp_pass(s, m == -INFINITY ? 0.f : -m);
+        float sum = exp_pass(s, m == -INFINITY ? 0.f : -m, upper_in_flight);
         float acc = 1.f;
         bool any_need = false;
         if (__any_sync(0xffffffffu, !(sum <= P_SUM_BOUND) || m == -INFINITY)) {

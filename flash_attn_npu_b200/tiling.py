@@ -12,11 +12,10 @@ Meaning of the knobs on sm_100a:
                    sharing each K/V tile, ping-ponged between two softmax warpgroups)
   BLOCK_N          keys per pipeline step: 64 or 128 (N of the Q.K^T MMA)
   NUM_STAGES       depth of the K/V shared-memory ring (each stage holds one K or one V tile)
-  PERSISTENT_CTAS  > 0: run the persistent kernel (fp16/bf16, head_dim 64/128, 256 x 128) on a
-                   grid of that many CTAs, each looping over tiles.  0: library default --
-                   the persistent kernel (one CTA per SM) for causal masks, one CTA per tile
-                   otherwise.  Configurations the persistent kernel does not serve refuse a
-                   non-zero value.
+  PERSISTENT_CTAS  grid of the persistent kernel, which runs every fp16/bf16 call at head_dim
+                   64/128 with the 256 x 128 tile: each CTA loops over tiles; 0 = one CTA per
+                   SM.  Other configurations run one CTA per tile and refuse a non-zero
+                   value.
 """
 from __future__ import annotations
 
@@ -80,12 +79,10 @@ def persistent_kernel_shape(head_dim: int, dtype, cfg: TileConfig) -> bool:
             and cfg.block_m == 256 and cfg.block_n == 128)
 
 
-def persistent_kernel_serves(head_dim: int, dtype, cfg: TileConfig, causal: bool,
-                             sm_scale: float = 1.0) -> bool:
+def persistent_kernel_serves(head_dim: int, dtype, cfg: TileConfig, sm_scale: float = 1.0) -> bool:
     """True when a call runs on the persistent kernel (mirrors `use_ws` in csrc/fa_fwd_api.cu):
-    a shape it serves, a positive scale, and either PERSISTENT_CTAS > 0 or a causal mask."""
-    return (persistent_kernel_shape(head_dim, dtype, cfg) and sm_scale > 0
-            and (cfg.persistent_ctas > 0 or bool(causal)))
+    a shape it serves and a positive scale."""
+    return persistent_kernel_shape(head_dim, dtype, cfg) and sm_scale > 0
 
 
 def geometry(head_dim: int, dtype, cfg: TileConfig) -> dict | None:

@@ -69,12 +69,11 @@ typedef struct FaTileConfig {
   int32_t block_m;         /* query rows per CTA: 128 or 256 (two 128-row tiles) */
   int32_t block_n;         /* keys per pipeline step: 64 or 128 */
   int32_t num_stages;      /* K/V shared-memory ring depth; 0 = largest that fits */
-  int32_t persistent_ctas; /* > 0: run the persistent kernel with a grid of this many CTAs,
-                              each looping over tiles (reference PERSISTENT_PROGRAMS); refused
-                              (FA_ERR_UNSUPPORTED_TILE) where that kernel does not serve the call
-                              (it serves fp16 / bf16, head_dim 64 / 128, block 256 x 128,
-                              sm_scale > 0).  0: library default -- the persistent kernel with
-                              one CTA per SM for causal masks, one CTA per tile otherwise. */
+  int32_t persistent_ctas; /* grid of the persistent kernel, which runs every call it serves
+                              (fp16 / bf16, head_dim 64 / 128, block 256 x 128, sm_scale > 0):
+                              each CTA loops over tiles (reference PERSISTENT_PROGRAMS); 0 = one
+                              CTA per SM.  Non-zero values are refused (FA_ERR_UNSUPPORTED_TILE)
+                              for calls that run one CTA per tile. */
 } FaTileConfig;
 
 typedef struct FaFwdArgs {

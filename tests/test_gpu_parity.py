@@ -384,9 +384,8 @@ def test_persistent_grid_sizes(head_dim, causal, ctas, cuda_device):
     tiles = B * H * 4
     assert ops.grid_size(B, H, S, head_dim, torch.bfloat16, causal, 256, 128, ctas) == min(
         tiles, ctas)
-    # library default: persistent (one CTA per SM) for causal masks, one CTA per tile otherwise
-    assert ops.grid_size(B, H, S, head_dim, torch.bfloat16, causal, 256, 128) == (
-        min(tiles, sms) if causal else tiles)
+    # library default: one CTA per SM; one CTA per tile when asked for
+    assert ops.grid_size(B, H, S, head_dim, torch.bfloat16, causal, 256, 128) == min(tiles, sms)
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])

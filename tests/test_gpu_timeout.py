@@ -4,8 +4,9 @@ The test library `libfa_sm100_shortwait.so` is the product source built with a p
 limit of zero (`python -m flash_attn_npu_b200.build --variant shortwait`): any mbarrier wait
 that is not satisfied after its first polls gives up, records FA_ERR_DEVICE_TIMEOUT in the
 status word and raises the CTA's abort flag; every role then drains its own in-flight TMA
-loads and MMAs (that limit stays long) and the CTA exits.  On a launch of 1024 CTAs some wait
-is certain to give up.  The child process checks that
+loads and MMAs (that limit stays long) and the CTA exits.  On a launch of 1024 query blocks
+some wait is certain to give up.  Both kernels are exercised: the persistent one (grid = one CTA
+per SM, each looping over tiles) and the one-CTA-per-tile one.  The child process checks that
 
   - the launch returns and the stream synchronizes (nothing hangs),
   - the status word reads FA_ERR_DEVICE_TIMEOUT,
@@ -28,7 +29,7 @@ from conftest import REPO
 pytestmark = pytest.mark.gpu
 
 
-def _child_main() -> None:
+def _child_main(kernel: str) -> None:
     from flash_attn_npu_b200 import _native, build, ops
     from oracle.attention_ref import attention_ref_torch
 
@@ -48,7 +49,13 @@ def _child_main() -> None:
                              o_ptr=out.data_ptr(), lse_ptr=lse.data_ptr(), batch=B, heads=H,
                              seqlen=S, head_dim=D, q_stride=st, k_stride=st, v_stride=st,
                              o_stride=st, dtype_code=_native.FA_DTYPE_BF16, causal=False,
-                             sm_scale=D ** -0.5, status_ptr=status.data_ptr())
+                             sm_scale=D ** -0.5, status_ptr=status.data_ptr(),
+                             block_m=256, block_n=128,
+                             persistent_ctas=(torch.cuda.get_device_properties(dev)
+                                              .multi_processor_count
+                                              if kernel == "persistent" else 0),
+                             flags=(_native.FA_FLAG_ONE_CTA_PER_TILE
+                                    if kernel == "one_cta_per_tile" else 0))
     rc = lib.fa_fwd_sm100(ctypes.byref(args),
                           ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
     torch.cuda.synchronize(dev)
@@ -65,10 +72,12 @@ def _child_main() -> None:
         "after_lse_abs": (l2.cpu() - rl).abs().max().item()}), flush=True)
 
 
-def test_pipeline_wait_timeout_reports_status_and_context_survives(native_lib, cuda_device):
+@pytest.mark.parametrize("kernel", ["persistent", "one_cta_per_tile"])
+def test_pipeline_wait_timeout_reports_status_and_context_survives(kernel, native_lib,
+                                                                    cuda_device):
     from flash_attn_npu_b200 import _native, build
     build.build(variant="shortwait")  # no-op when up to date
-    res = subprocess.run([sys.executable, __file__, "child"], cwd=str(REPO),
+    res = subprocess.run([sys.executable, __file__, "child", kernel], cwd=str(REPO),
                          env=dict(os.environ), capture_output=True, text=True, timeout=300)
     assert res.returncode == 0, res.stderr[-3000:]
     line = [ln for ln in res.stdout.splitlines() if ln.startswith("RESULT ")][-1]
@@ -82,4 +91,4 @@ def test_pipeline_wait_timeout_reports_status_and_context_survives(native_lib, c
 if __name__ == "__main__":
     if len(sys.argv) > 1 and sys.argv[1] == "child":
         sys.path.insert(0, str(REPO))
-        _child_main()
+        _child_main(sys.argv[2])

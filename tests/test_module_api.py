@@ -72,13 +72,12 @@ def test_tiling_defaults_and_sources():
     rt = fam._describe_runtime(16, 16, 8192, 128, False)
     assert rt["selected_config"] == {"BLOCK_M": 256, "BLOCK_N": 128}
     assert rt["total_tiles"] == 32 * 256 and rt["stage"] == 1
-    # cfg4 (non-causal) runs one CTA per tile by default, on a 4-deep K/V ring (the ring depth
-    # of a 256 x 128 tile is the one both kernels can hold)
+    # cfg4 runs on the persistent kernel: a 4-deep K/V ring, one CTA per SM looping over tiles
     assert rt["pipeline"]["NUM_STAGES"] == 4
-    assert rt["kernel"] == "one CTA per tile"
-    assert rt["launched_programs"] == rt["total_tiles"]
+    assert rt["kernel"] == "persistent"
+    assert rt["launched_programs"] == min(rt["total_tiles"], fam._sm_count())
     assert fam._build_grid(16, 16, 8192, 256) == (8192, 1, 1)
-    # the same shape with a causal mask runs on the persistent kernel, one CTA per SM
+    # so does the same shape with a causal mask
     rtc = fam._describe_runtime(16, 16, 8192, 128, True)
     assert rtc["kernel"] == "persistent"
     assert rtc["launched_programs"] == min(rtc["total_tiles"], fam._sm_count())
