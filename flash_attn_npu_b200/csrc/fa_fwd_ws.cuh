@@ -641,13 +641,19 @@ __global__ void __launch_bounds__(512, 1)
     };
     // Hands this step's per-row rescale factors to the correction warp (once it has read the
     // previous step's).
-    auto give_stats = [&](float acc) {
+    // Every step after the first hands its per-row rescale factors to the correction warp
+    // exactly once (1 for a row whose base stayed).  The wait for the slot (the correction warp
+    // has read the previous step's factors) is taken at the top of the step, while S is still
+    // being computed, so giving the factors costs only the store and the arrival.
+    auto stats_slot = [&]() {
       if (!ws_wait(sh, smem_u32(&sh->stats_free[i]), xf_ph ^ 1u, p.status)) return false;
       xf_ph ^= 1u;
+      return true;
+    };
+    auto give_stats = [&](float acc) {
       sh->acc_scale[i][r] = acc;
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&sh->stats[i]));
-      return true;
     };
 
     for (int t = t_first; t < p.total_tiles && ok; t += t_step) {
@@ -721,6 +727,8 @@ __global__ void __launch_bounds__(512, 1)
       // move, so the rest of the tile takes the max first.
       int j = 1;
       for (; j < nk; ++j) {
+        ok = stats_slot();
+        if (!ok) break;
         const bool upper_in_flight = load_s_lower(j);
         if (!ok) break;
         float sum = exp_pass(s, m == -INFINITY ? 0.f : -m, upper_in_flight);
@@ -735,8 +743,7 @@ __global__ void __launch_bounds__(512, 1)
               acc = ex2_approx(m - mx);  // m = -inf gives 0
               m = mx;
             }
-            ok = give_stats(acc);
-            if (!ok) break;
+            give_stats(acc);
             tmem_wait_st();  // the first pass's P stores land before they are overwritten
             sum = exp_pass(s, m == -INFINITY ? 0.f : -m);
           }
@@ -744,8 +751,7 @@ __global__ void __launch_bounds__(512, 1)
         release(any_need ? 1u : 2u);
         l = l * acc + sum;
         if (!any_need) {
-          ok = give_stats(1.f);
-          if (!ok) break;
+          give_stats(1.f);
         } else if (FA_WS_ADAPTIVE) {
           ++j;
           break;
@@ -755,6 +761,8 @@ __global__ void __launch_bounds__(512, 1)
       // ---- the rest of the tile: row max first, then the exponentials against the chosen
       // base; a base move costs the correction warp's O rescale, overlapped with this pass
       for (; j < nk; ++j) {
+        ok = stats_slot();
+        if (!ok) break;
         ok = load_s(j);
         if (!ok) break;
         const float mx = row_max<128>(s) * sl2;
@@ -765,17 +773,11 @@ __global__ void __launch_bounds__(512, 1)
           m = mx;
         }
         const bool any_need = __any_sync(0xffffffffu, need);
-        if (any_need) {
-          ok = give_stats(acc);
-          if (!ok) break;
-        }
+        if (any_need) give_stats(acc);
         const float sum = exp_pass(s, m == -INFINITY ? 0.f : -m);
         release(any_need ? 1u : 2u);
         l = l * acc + sum;
-        if (!any_need) {
-          ok = give_stats(1.f);
-          if (!ok) break;
-        }
+        if (!any_need) give_stats(1.f);
       }
       if (!ok) break;
       // tile done: logsumexp, and 1/l for the correction warps' epilogue (once they have read

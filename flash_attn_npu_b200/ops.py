@@ -121,6 +121,55 @@ def _tma_view(t: torch.Tensor) -> torch.Tensor:
     return t if _tma_ok(t) else t.contiguous()
 
 
+# Launch fast path.  A call whose layout was validated and launched once before -- same shapes,
+# strides, dtypes, device, mask, scale and tile knobs, fresh outputs, the per-device status
+# word -- reuses that call's prepared argument block and only fills in this call's pointers,
+# which keeps the host cost of a launch below the kernel time of small problems (at B4 H16 S1024
+# D64 the full path costs about as much host time as the kernel takes on the device).
+_FAST: dict = {}
+_FAST_LIMIT = 256
+_PTR_FIELDS = ("q", "k", "v", "o", "lse")
+
+
+class _FastEntry:
+    __slots__ = ("args", "lse_shape", "device", "index")
+
+    def __init__(self, args, lse_shape, device, index):
+        self.args = args            # FaFwdArgs of the validated call (its status word included)
+        self.lse_shape = lse_shape
+        self.device = device
+        self.index = index
+
+
+def _fast_key(q, k, v, causal, sm_scale, block_m, block_n, num_stages, persistent_ctas,
+              fp32_tf32, one_cta_per_tile):
+    return (q.shape, q.stride(), k.shape, k.stride(), v.shape, v.stride(), q.dtype, k.dtype,
+            v.dtype, q.device, k.device, v.device, bool(causal), float(sm_scale), block_m,
+            block_n, num_stages, persistent_ctas, bool(fp32_tf32), bool(one_cta_per_tile))
+
+
+def _fast_launch(ent: _FastEntry, q, k, v):
+    """(out, lse), or None when this call needs the full path (a misaligned pointer, another
+    current device, or a launch error, which the full path reports)."""
+    qp, kp, vp = q.data_ptr(), k.data_ptr(), v.data_ptr()
+    if (qp | kp | vp) & 15 or torch.cuda.current_device() != ent.index:
+        return None
+    out = torch.empty_like(q)
+    lse = torch.empty(ent.lse_shape, device=ent.device, dtype=torch.float32)
+    op, lp = out.data_ptr(), lse.data_ptr()
+    if op & 15:
+        return None
+    args = _native.FaFwdArgs.from_buffer_copy(ent.args)
+    args.q, args.k, args.v, args.o, args.lse = qp, kp, vp, op, lp
+    try:
+        _native.launch(args, torch.cuda.current_stream(ent.device).cuda_stream)
+    except _native.NativeError:
+        return None
+    if _CHECK_EVERY_CALL:
+        check_device_status(ent.device)
+    return out, lse
+
+
 def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_scale: float, *,
             block_m: int = 0, block_n: int = 0, num_stages: int = 0, persistent_ctas: int = 0,
             out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
@@ -139,6 +188,15 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_
     256 x 128 tile run on the persistent kernel (grid `persistent_ctas`, 0 = one CTA per SM)
     unless `one_cta_per_tile` asks for the other kernel.
     """
+    fast_key = None
+    if out is None and lse is None and status is None:
+        fast_key = _fast_key(q, k, v, causal, sm_scale, block_m, block_n, num_stages,
+                             persistent_ctas, fp32_tf32, one_cta_per_tile)
+        ent = _FAST.get(fast_key)
+        if ent is not None:
+            res = _fast_launch(ent, q, k, v)
+            if res is not None:
+                return res
     validate_inputs(q, k, v)
     z, h, n_ctx, head_dim = q.shape
     code = dtype_code(q.dtype)
@@ -191,6 +249,11 @@ def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sm_
             raise
     if own_status and status is not None and _CHECK_EVERY_CALL:
         check_device_status(q.device)
+    if (fast_key is not None and status is not None and qv is q and kv is k and vv is v
+            and out.stride() == q.stride() and len(_FAST) < _FAST_LIMIT):
+        # this layout launched: later calls with the same key take the fast path
+        _FAST[fast_key] = _FastEntry(_native.FaFwdArgs.from_buffer_copy(args), (z, h, n_ctx),
+                                     q.device, _device_index(q.device))
     return out, lse
 
 

@@ -302,6 +302,38 @@ def test_preallocated_outputs_and_determinism(cuda_device):
     assert torch.equal(o1, o2) and torch.equal(l1, l2)
 
 
+def test_launch_fast_path_matches_full_path(cuda_device):
+    """A repeated launch layout takes the cached fast path: same results as the full path, new
+    pointers filled in, and a different layout (other strides, other tile) is not confused
+    with it."""
+    B, H, S, D = 2, 3, 300, 64
+    q, k, v = (_rand((B, H, S, D), torch.bfloat16, s, "cuda") for s in (70, 71, 72))
+    key = ops._fast_key(q, k, v, False, 0.125, 0, 0, 0, 0, False, False)
+    ops._FAST.pop(key, None)
+    o1, l1 = ops.forward(q, k, v, False, 0.125)          # full path; caches the layout
+    assert key in ops._FAST
+    o2, l2 = ops.forward(q, k, v, False, 0.125)          # fast path
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2) and torch.equal(l1, l2)
+    assert o2.data_ptr() != o1.data_ptr()                # fresh outputs every call
+    q2 = _rand((B, H, S, D), torch.bfloat16, 73, "cuda")  # same layout, other tensor
+    o3, l3 = ops.forward(q2, k, v, False, 0.125)
+    ro, rl = attention_ref_torch(q2.cpu(), k.cpu(), v.cpu(), False, 0.125)
+    torch.cuda.synchronize()
+    _check(o3, l3, ro, rl)
+    # BSHD views of the same data: other strides, so the full path runs and is correct
+    qb, kb, vb = (t.transpose(1, 2).contiguous().transpose(1, 2) for t in (q, k, v))
+    o4, l4 = ops.forward(qb, kb, vb, False, 0.125)
+    o5, l5 = ops.forward(qb, kb, vb, False, 0.125)       # and then its own fast path
+    torch.cuda.synchronize()
+    assert o4.stride() == qb.stride()
+    assert torch.equal(o4, o1) and torch.equal(l4, l1) and torch.equal(o5, o1)
+    # another tile for the same tensors is another layout key
+    o6, l6 = ops.forward(q, k, v, False, 0.125, block_m=128, block_n=64)
+    torch.cuda.synchronize()
+    _check(o6, l6, *attention_ref_torch(q.cpu(), k.cpu(), v.cpu(), False, 0.125))
+
+
 def test_module_api_on_gpu(cuda_device):
     import flash_attention_forward as fam
     q, k, v = fam._make_inputs(2, 2, 257, 64, torch.float16)
