@@ -47,7 +47,7 @@ DEFAULT_TILING_PRESETS = {
     (128, 8, 2048, 128, True): (256, 128, 4, 0),
     (128, 8, 2048, 256, False): (128, 128, 2, 0),
     (128, 8, 4096, 128, False): (256, 128, 4, 0),
-    (128, 8, 8192, 64, False): (256, 128, 6, 0),
+    (128, 8, 8192, 64, False): (256, 128, 5, 0),
 }
 # END AUTO-TUNED DEFAULT TILING PRESETS
 
