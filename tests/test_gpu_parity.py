@@ -179,19 +179,18 @@ def test_cfg3_full_causal_with_lse(cuda_device):
     _config_check("cfg3")
 
 
-def test_cfg4_sampled_slices(cuda_device):
-    # 256 slices of S=8192: check 12 spread over the batch, plus whole-tensor properties
-    sl = [(b, h) for b, h in [(0, 0), (0, 15), (3, 7), (5, 1), (7, 8), (8, 3), (9, 12),
-                              (11, 0), (12, 5), (13, 14), (14, 9), (15, 15)]]
-    q, k, v, out, lse, _ = _config_check("cfg4", sl)
+def test_cfg4_every_slice(cuda_device):
+    # all 256 slices of S=8192 against the fp32 oracle (evaluated per slice on the GPU), plus
+    # whole-tensor properties
+    q, k, v, out, lse, _ = _config_check("cfg4")
     assert torch.isfinite(out.float()).all() and torch.isfinite(lse).all()
     # size-independent properties: |O| <= max|V| per slice; LSE >= log-mean-exp lower bound
     assert (out.float().abs().amax(dim=(2, 3)) <= v.float().abs().amax(dim=(2, 3)) + 1e-2).all()
 
 
-def test_cfg5_outliers_sampled_slices(cuda_device):
-    sl = [(0, 0), (0, 31), (0, 63), (1, 5), (1, 40), (1, 63)]
-    q, k, v, out, lse, _ = _config_check("cfg5", sl)
+def test_cfg5_outliers_every_slice(cuda_device):
+    # all 128 slices of S=16384 (causal, 1 % of q and k rows scaled by 20)
+    q, k, v, out, lse, _ = _config_check("cfg5")
     assert torch.isfinite(out.float()).all() and torch.isfinite(lse).all()
     # causal row 0 attends only key 0
     torch.testing.assert_close(out[:, :, 0].float(), v[:, :, 0].float(), atol=1e-3, rtol=0)
@@ -372,8 +371,8 @@ def test_reference_evaluator_correctness_cases(case, dtype, cuda_device):
 def test_reference_evaluator_performance_shapes_at_preset_tiles(idx, dtype, cuda_device):
     """The evaluator's six performance shapes at full size, through the module API with the
     tuned preset each one selects, and with the evaluator's own seeds (seed + 18 + idx) and
-    input recipe.  The evaluator checks every performance case before timing it; here sampled
-    (b, h) slices are held to the parity bar (and to the evaluator's allclose rule)."""
+    input recipe.  The evaluator checks every performance case before timing it; here every
+    (b, h) slice is held to the parity bar (and to the evaluator's allclose rule)."""
     import flash_attention_forward as fam
     z, h, n, d, causal = fa_inputs.EVALUATOR_PERFORMANCE_CASES[idx]
     assert fam.get_tiling_source(z, h, n, d, causal) == "preset"
@@ -382,7 +381,7 @@ def test_reference_evaluator_performance_shapes_at_preset_tiles(idx, dtype, cuda
     out, lse = fam.attention(q, k, v, causal, 0.5, return_lse=True)
     torch.cuda.synchronize()
     assert torch.isfinite(out.float()).all() and torch.isfinite(lse).all()
-    for b, hh in [(0, 0), (z // 3, h - 1), ((2 * z) // 3, h // 2), (z - 1, 1)]:
+    for b, hh in [(b, hh) for b in range(z) for hh in range(h)]:
         ro, rl = attention_ref_torch(q[b, hh], k[b, hh], v[b, hh], causal, 0.5)
         _check(out[b, hh], lse[b, hh], ro, rl)
         assert torch.allclose(ro.to(dtype), out[b, hh], atol=1e-2, rtol=1e-2)

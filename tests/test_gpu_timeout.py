@@ -29,7 +29,7 @@ from conftest import REPO
 pytestmark = pytest.mark.gpu
 
 
-def _child_main(kernel: str) -> None:
+def _child_main(kernel: str, head_dim: int) -> None:
     from flash_attn_npu_b200 import _native, build, ops
     from oracle.attention_ref import attention_ref_torch
 
@@ -38,7 +38,7 @@ def _child_main(kernel: str) -> None:
     lib.fa_fwd_sm100.restype = ctypes.c_int
     dev = torch.device("cuda", 0)
     g = torch.Generator().manual_seed(11)
-    B, H, S, D = 4, 16, 4096, 128
+    B, H, S, D = 4, 16, 4096, head_dim
     q, k, v = (torch.randn((B, H, S, D), generator=g).to(torch.bfloat16).to(dev)
                for _ in range(3))
     out = torch.empty_like(q)
@@ -72,12 +72,16 @@ def _child_main(kernel: str) -> None:
         "after_lse_abs": (l2.cpu() - rl).abs().max().item()}), flush=True)
 
 
-@pytest.mark.parametrize("kernel", ["persistent", "one_cta_per_tile"])
-def test_pipeline_wait_timeout_reports_status_and_context_survives(kernel, native_lib,
+# head_dim 64 runs the persistent kernel's separate-P protocol (S read -> next S, P V -> next P
+# store), head_dim 128 the one with P over S
+@pytest.mark.parametrize("kernel,head_dim", [("persistent", 128), ("persistent", 64),
+                                             ("one_cta_per_tile", 128)])
+def test_pipeline_wait_timeout_reports_status_and_context_survives(kernel, head_dim, native_lib,
                                                                     cuda_device):
     from flash_attn_npu_b200 import _native, build
     build.build(variant="shortwait")  # no-op when up to date
-    res = subprocess.run([sys.executable, __file__, "child", kernel], cwd=str(REPO),
+    res = subprocess.run([sys.executable, __file__, "child", kernel, str(head_dim)],
+                         cwd=str(REPO),
                          env=dict(os.environ), capture_output=True, text=True, timeout=300)
     assert res.returncode == 0, res.stderr[-3000:]
     line = [ln for ln in res.stdout.splitlines() if ln.startswith("RESULT ")][-1]
@@ -91,4 +95,4 @@ def test_pipeline_wait_timeout_reports_status_and_context_survives(kernel, nativ
 if __name__ == "__main__":
     if len(sys.argv) > 1 and sys.argv[1] == "child":
         sys.path.insert(0, str(REPO))
-        _child_main(sys.argv[2])
+        _child_main(sys.argv[2], int(sys.argv[3]))
