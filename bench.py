@@ -212,6 +212,23 @@ def kernel_label(cfg, fam):
     return "fa_fwd_sm100_kernel (one CTA per tile, one launch per step)"
 
 
+XU_EX2_PER_CLK_PER_SM = 16
+
+
+def xu_roofline(n_slices, cfg, ms, clocks, dev):
+    """Exponentials per second against the exp2 unit's throughput: one exp per (query, key)
+    pair, S^2 per (b, h) slice, S (S + 1) / 2 under a causal mask."""
+    S = cfg.seqlen
+    exps = n_slices * (S * (S + 1) / 2 if cfg.causal else S * S)
+    mhz = (clocks or {}).get("sm_mhz") or (clocks or {}).get("sm_max_mhz") or 1965.0
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    peak = XU_EX2_PER_CLK_PER_SM * sms * mhz * 1e6 / 1e12
+    achieved = exps / (ms * 1e-3) / 1e12
+    return {"bound": "xu", "achieved": achieved, "peak": peak, "unit": "Texp/s",
+            "frac": achieved / peak, "exps_per_launch": exps,
+            "peak_source": f"{XU_EX2_PER_CLK_PER_SM} ex2/clk/SM x {sms} SMs x {mhz:.0f} MHz"}
+
+
 def fa_flops_local(q, cfg):
     n = q.shape[0] * q.shape[1]
     f = 4.0 * n * cfg.seqlen * cfg.seqlen * cfg.head_dim
@@ -498,6 +515,11 @@ def run_ours(args, cfg, world, rank, local):
                          "peak_source": f"{peak_src} bf16 dense (burst)",
                          "traffic": traffic,
                          "kernel": kernel_label(cfg, fam)},
+            # second limit of this kernel: the exp2 unit (16 ex2.approx results per clock per SM,
+            # measured on B200), against the median SM clock sampled during the timed region
+            # (nvidia-smi's figure, above the effective clock under the power cap, so this
+            # fraction is a lower bound)
+            "roofline_xu": xu_roofline(n_local, cfg, local_ms, clocks, dev),
             "clocks": clocks,
             "cpu_baseline": cpu_baseline,
             "context_library_kernel": library,
